@@ -1,0 +1,1163 @@
+// Host pipeline of the engine: operand staging, transpose for A*A^T, the analyze -> symbolic ->
+// scan -> numeric sequence, the ESC baseline flow, pools, error handling and phase timing.
+//
+// Reference counterparts: hash_product (spgemm_kernel_hash.cu:813-1109), merge3_product
+// (spgemm_merge.cu:760-933), spgemm_self_product_manual (spgemm_kernel_manual.cu:272-437) and
+// the pools of src/mempool.cu. Differences that matter to callers:
+//   * one host synchronisation inside the pipeline (to size C), instead of one per phase;
+//   * all temporaries come from a CUDA stream-ordered memory pool (release threshold raised, so
+//     steady-state calls do no driver allocation);
+//   * every failure returns a status instead of exiting the process.
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "kernels.cuh"
+
+namespace appt {
+
+// ------------------------------------------------------------------ errors and counters
+static thread_local std::string t_last_error;
+void set_error(const std::string& m) { t_last_error = m; }
+const char* last_error() { return t_last_error.c_str(); }
+
+static std::atomic<long long> g_launches{0};
+long long kernel_launches() { return g_launches.load(); }
+void note_launches(long long n) { g_launches += n; }
+
+#define CK(call)                                                                          \
+  do {                                                                                    \
+    cudaError_t e_ = (call);                                                              \
+    if (e_ != cudaSuccess) {                                                              \
+      set_error(std::string(#call) + ": " + cudaGetErrorString(e_));                      \
+      return e_ == cudaErrorMemoryAllocation ? kErrOom : kErrCuda;                        \
+    }                                                                                     \
+  } while (0)
+
+static bool env_flag(const char* k) {
+  const char* e = std::getenv(k);
+  return e && *e && std::atoi(e) > 0;
+}
+
+int device_count() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+// ------------------------------------------------------------------ per-device context
+struct DeviceCtx {
+  int device = -1;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;
+  cudaMemPool_t pool = nullptr;
+  char* stage = nullptr;   // pinned host staging for small device->host reads
+  std::mutex mu;
+  bool ok = false;
+};
+
+static DeviceCtx g_ctx[64];
+static std::mutex g_ctx_mu;
+
+static int get_ctx(int device, DeviceCtx** out) {
+  if (device < 0 || device >= 64) {
+    set_error("device ordinal out of range");
+    return kErrInvalid;
+  }
+  std::lock_guard<std::mutex> g(g_ctx_mu);
+  DeviceCtx& c = g_ctx[device];
+  if (!c.ok) {
+    const int n = device_count();
+    if (n == 0) {
+      set_error("no CUDA device");
+      return kErrNoDevice;
+    }
+    if (device >= n) {
+      set_error("device ordinal beyond the device count");
+      return kErrInvalid;
+    }
+    CK(cudaSetDevice(device));
+    CK(cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, device));
+    CK(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    cudaMemPoolProps props;
+    std::memset(&props, 0, sizeof(props));
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    CK(cudaMemPoolCreate(&c.pool, &props));
+    unsigned long long thr = ~0ull;
+    CK(cudaMemPoolSetAttribute(c.pool, cudaMemPoolAttrReleaseThreshold, &thr));
+    CK(cudaMallocHost((void**)&c.stage, 4096));
+    c.device = device;
+    c.ok = true;
+  }
+  *out = &c;
+  return kOk;
+}
+
+// Stream-ordered scratch allocations freed when the object goes out of scope, unless detached.
+struct Scratch {
+  DeviceCtx* ctx;
+  cudaStream_t s;
+  std::vector<void*> ptrs;
+  bool failed = false;
+  Scratch(DeviceCtx* c, cudaStream_t st) : ctx(c), s(st) {}
+  template <typename T>
+  T* get(size_t count) {
+    size_t bytes = count * sizeof(T);
+    if (bytes == 0) bytes = 256;
+    void* p = nullptr;
+    if (cudaMallocFromPoolAsync(&p, bytes, ctx->pool, s) != cudaSuccess) {
+      cudaGetLastError();
+      failed = true;
+      return nullptr;
+    }
+    ptrs.push_back(p);
+    return reinterpret_cast<T*>(p);
+  }
+  void detach(void* p) {
+    for (auto& q : ptrs)
+      if (q == p) q = nullptr;
+  }
+  ~Scratch() {
+    for (void* p : ptrs)
+      if (p) cudaFreeAsync(p, s);
+  }
+};
+
+// ------------------------------------------------------------------ phase timing
+struct PhaseTimer {
+  bool on = false;
+  cudaStream_t s = nullptr;
+  struct Mark {
+    int phase;
+    cudaEvent_t a, b;
+  };
+  std::vector<Mark> marks;
+  cudaEvent_t t0 = nullptr, t1 = nullptr;
+  int cur = -1;
+  cudaEvent_t cur_a = nullptr;
+  void start(bool enable, cudaStream_t st) {
+    on = enable;
+    s = st;
+    if (!on) return;
+    cudaEventCreate(&t0);
+    cudaEventCreate(&t1);
+    cudaEventRecord(t0, s);
+  }
+  void begin(int phase) {
+    if (!on) return;
+    end();
+    cur = phase;
+    cudaEventCreate(&cur_a);
+    cudaEventRecord(cur_a, s);
+  }
+  void end() {
+    if (!on || cur < 0) return;
+    cudaEvent_t b;
+    cudaEventCreate(&b);
+    cudaEventRecord(b, s);
+    marks.push_back({cur, cur_a, b});
+    cur = -1;
+  }
+  void finish(CallStats* st) {
+    if (!on) return;
+    end();
+    cudaEventRecord(t1, s);
+    cudaEventSynchronize(t1);
+    float ms = 0.f;
+    if (st) {
+      cudaEventElapsedTime(&ms, t0, t1);
+      st->ms_total = ms;
+      for (int i = 0; i < 8; ++i) st->ms_phase[i] = 0.0;
+      for (auto& m : marks) {
+        cudaEventElapsedTime(&ms, m.a, m.b);
+        st->ms_phase[m.phase] += ms;
+      }
+    }
+    for (auto& m : marks) {
+      cudaEventDestroy(m.a);
+      cudaEventDestroy(m.b);
+    }
+    marks.clear();
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    on = false;
+  }
+  ~PhaseTimer() {
+    if (on) finish(nullptr);
+  }
+};
+
+enum Phase { kPhH2D = 0, kPhTranspose, kPhAnalyze, kPhSymbolic, kPhScan, kPhNumeric, kPhD2H, kPhOther };
+static const char* kPhaseNames[8] = {"h2d", "transpose", "analyze", "symbolic",
+                                     "scan", "numeric",   "d2h",     "other"};
+
+// ------------------------------------------------------------------ device pipeline
+struct DevC {            // device-resident result, allocations owned by the pool
+  long long rows = 0, cols = 0, nnz = 0;
+  long long* rp = nullptr;
+  int* ci = nullptr;
+  double* val = nullptr;
+};
+
+static int lanes_per_row(long long nnz, long long rows) {
+  const double avg = rows > 0 ? (double)nnz / (double)rows : 0.0;
+  if (avg <= 6) return 4;
+  if (avg <= 12) return 8;
+  if (avg <= 24) return 16;
+  return 32;
+}
+
+static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
+                      cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C, CallStats* st) {
+  const int m = A.rows;
+  const int sms = ctx->num_sms;
+  long long* flop = sc.get<long long>(m);
+  int* lo = sc.get<int>(m);
+  int* hi = sc.get<int>(m);
+  uint8_t* key = sc.get<uint8_t>(m);
+  int* row_nnz = sc.get<int>(m);
+  long long* foff = sc.get<long long>((size_t)m + 1);
+  long long* crp = sc.get<long long>((size_t)m + 1);
+  long long* scs = sc.get<long long>(scan_scratch_elems(m));
+  AnalyzeStats* gst = sc.get<AnalyzeStats>(1);
+  int* err = sc.get<int>(4);
+  if (sc.failed) {
+    set_error("device pool allocation failed");
+    return kErrOom;
+  }
+  CK(cudaMemsetAsync(gst, 0, sizeof(AnalyzeStats), s));
+  CK(cudaMemsetAsync(err, 0, sizeof(int) * 4, s));
+  tm.begin(kPhAnalyze);
+  launch_analyze(A, B, upper, row_base, kMethodEsc, lanes_per_row(a_nnz, m), flop, lo, hi, key,
+                 row_nnz, gst, err, sms, s);
+  note_launches(m > 0 ? 1 : 0);
+  scan_exclusive(flop, foff, m, scs, s);
+  note_launches(m > 0 ? 3 : 0);
+  CK(cudaMemcpyAsync(ctx->stage, foff + m, 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(ctx->stage + 64, gst, sizeof(AnalyzeStats), cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(ctx->stage + 128, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  long long P;
+  std::memcpy(&P, ctx->stage, 8);
+  AnalyzeStats hst;
+  std::memcpy(&hst, ctx->stage + 64, sizeof(hst));
+  int herr = 0;
+  std::memcpy(&herr, ctx->stage + 128, sizeof(int));
+  if (herr & kErrBounds) {
+    set_error("operand index out of range (A column >= B rows)");
+    return kErrInvalid;
+  }
+  if (st) st->products = (long long)hst.total_flop;
+  int* keys = sc.get<int>(P);
+  double* vals = sc.get<double>(P);
+  int* keys_alt = sc.get<int>(P);
+  double* vals_alt = sc.get<double>(P);
+  void* sss = sc.get<char>(segsort_scratch_bytes(m));
+  if (sc.failed) {
+    set_error("device pool allocation failed (ESC needs 24 bytes per intermediate product)");
+    return kErrOom;
+  }
+  tm.begin(kPhNumeric);
+  launch_esc_expand(A, B, upper, row_base, foff, keys, vals, sms, s);
+  segsort(keys, vals, keys_alt, vals_alt, foff, m, sss, sms, s);
+  launch_esc_count(m, foff, keys, row_nnz, sms, s);
+  note_launches(m > 0 ? 13 : 0);
+  tm.begin(kPhScan);
+  scan_exclusive(row_nnz, crp, m, scs, s);
+  note_launches(m > 0 ? 3 : 0);
+  CK(cudaMemcpyAsync(ctx->stage, crp + m, 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  long long nnz;
+  std::memcpy(&nnz, ctx->stage, 8);
+  int* cci = sc.get<int>(nnz);
+  double* cval = sc.get<double>(nnz);
+  if (sc.failed) {
+    set_error("device pool allocation failed for C");
+    return kErrOom;
+  }
+  tm.begin(kPhNumeric);
+  launch_esc_compress(m, foff, keys, vals, crp, cci, cval, sms, s);
+  note_launches(m > 0 ? 1 : 0);
+  tm.end();
+  sc.detach(crp);
+  sc.detach(cci);
+  sc.detach(cval);
+  C->rows = m;
+  C->cols = B.cols;
+  C->nnz = nnz;
+  C->rp = crp;
+  C->ci = cci;
+  C->val = cval;
+  if (st) {
+    st->c_nnz = nnz;
+    st->method_used = kMethodEsc;
+  }
+  return kOk;
+}
+
+static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
+                           int method, cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C,
+                           CallStats* st) {
+  if (method == kMethodEsc)
+    return esc_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st);
+  const int m = A.rows;
+  const int sms = ctx->num_sms;
+  constexpr int kSymMergeBin = kNumSymBins;
+  const int nsb = kNumSymBins + 1;
+  long long* flop = sc.get<long long>(m);
+  int* lo = sc.get<int>(m);
+  int* hi = sc.get<int>(m);
+  uint8_t* symkey = sc.get<uint8_t>(m);
+  uint8_t* numkey = sc.get<uint8_t>(m);
+  int* row_nnz = sc.get<int>(m);
+  int* rows_sym = sc.get<int>(m);
+  int* rows_num = sc.get<int>(m);
+  long long* crp = sc.get<long long>((size_t)m + 1);
+  long long* boff_sym = sc.get<long long>(kMaxBins + 1);
+  long long* boff_num = sc.get<long long>(kMaxBins + 1);
+  AnalyzeStats* gst = sc.get<AnalyzeStats>(1);
+  int* err = sc.get<int>(4);
+  long long* scs = sc.get<long long>(scan_scratch_elems(m));
+  void* pscr = sc.get<char>(partition_scratch_bytes(m, kMaxBins));
+  if (sc.failed) {
+    set_error("device pool allocation failed");
+    return kErrOom;
+  }
+  CK(cudaMemsetAsync(gst, 0, sizeof(AnalyzeStats), s));
+  CK(cudaMemsetAsync(err, 0, sizeof(int) * 4, s));
+
+  tm.begin(kPhAnalyze);
+  launch_analyze(A, B, upper, row_base, method, lanes_per_row(a_nnz, m), flop, lo, hi, symkey,
+                 row_nnz, gst, err, sms, s);
+  partition_rows(symkey, m, nsb, rows_sym, boff_sym, pscr, s);
+  note_launches(m > 0 ? 7 : 0);
+
+  tm.begin(kPhSymbolic);
+  if (m > 0) {
+    for (int b = 0; b < kNumSymBins; ++b)
+      launch_symbolic(b, rows_sym, boff_sym, A, B, upper, row_base, lo, hi, flop, row_nnz, err,
+                      sms, s);
+    note_launches(kNumSymBins);
+    if (method == kMethodMerge) {
+      launch_merge_count(rows_sym, boff_sym, kSymMergeBin, A, B, upper, row_base, row_nnz, err,
+                         sms, s);
+      note_launches(1);
+    }
+  }
+
+  tm.begin(kPhScan);
+  scan_exclusive(row_nnz, crp, m, scs, s);
+  launch_classify_numeric(A, m, method, flop, lo, hi, row_nnz, numkey, sms, s);
+  partition_rows(numkey, m, kNumNumBins, rows_num, boff_num, pscr, s);
+  note_launches(m > 0 ? 10 : 0);
+
+  // the one mid-pipeline synchronisation: C's size and the numeric bin sizes
+  char* stg = ctx->stage;
+  CK(cudaMemcpyAsync(stg, crp + m, 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(stg + 8, boff_num, 8 * (kNumNumBins + 1), cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(stg + 256, gst, sizeof(AnalyzeStats), cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(stg + 512, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  long long nnz;
+  long long boff[kNumNumBins + 1];
+  AnalyzeStats hst;
+  int herr;
+  std::memcpy(&nnz, stg, 8);
+  std::memcpy(boff, stg + 8, sizeof(boff));
+  std::memcpy(&hst, stg + 256, sizeof(hst));
+  std::memcpy(&herr, stg + 512, sizeof(int));
+  if (herr & kErrBounds) {
+    set_error("operand index out of range (A column >= B rows)");
+    return kErrInvalid;
+  }
+  if (herr) {
+    set_error("symbolic phase reported device error bits " + std::to_string(herr));
+    return kErrDevice;
+  }
+  if (st) {
+    st->products = (long long)hst.total_flop;
+    for (int b = 0; b < kNumNumBins && b < 16; ++b) st->bin_rows[b] = boff[b + 1] - boff[b];
+  }
+  int* cci = sc.get<int>(nnz);
+  double* cval = sc.get<double>(nnz);
+  if (sc.failed) {
+    set_error("device pool allocation failed for C (" + std::to_string(nnz) + " entries)");
+    return kErrOom;
+  }
+
+  tm.begin(kPhNumeric);
+  for (int b = 0; b < kNumNumBins; ++b) {
+    const long long nr = boff[b + 1] - boff[b];
+    if (nr <= 0) continue;
+    if (b == kNumMerge)
+      launch_merge_numeric(rows_num, boff_num, b, nr, A, B, upper, row_base, crp, cci, cval, err,
+                           sms, s);
+    else
+      launch_numeric(b, rows_num, boff_num, nr, A, B, upper, row_base, lo, hi, crp, cci, cval,
+                     err, sms, s);
+    note_launches(1);
+  }
+  tm.end();
+  CK(cudaMemcpyAsync(stg + 512, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  std::memcpy(&herr, stg + 512, sizeof(int));
+  if (herr) {
+    set_error("numeric phase reported device error bits " + std::to_string(herr));
+    return kErrDevice;
+  }
+  sc.detach(crp);
+  sc.detach(cci);
+  sc.detach(cval);
+  C->rows = m;
+  C->cols = B.cols;
+  C->nnz = nnz;
+  C->rp = crp;
+  C->ci = cci;
+  C->val = cval;
+  if (st) {
+    st->c_nnz = nnz;
+    st->method_used = method;
+  }
+  return kOk;
+}
+
+// ------------------------------------------------------------------ operand staging
+static int stage_operand(const MatView& M, Scratch& sc, cudaStream_t s, Csr* out) {
+  int* rp = sc.get<int>((size_t)M.rows + 1);
+  int* ci = sc.get<int>((size_t)M.nnz);
+  double* val = sc.get<double>((size_t)M.nnz);
+  if (sc.failed) {
+    set_error("device pool allocation failed for an operand");
+    return kErrOom;
+  }
+  CK(cudaMemcpyAsync(rp, M.rp, sizeof(int) * ((size_t)M.rows + 1), cudaMemcpyHostToDevice, s));
+  if (M.nnz > 0) {
+    CK(cudaMemcpyAsync(ci, M.ci, sizeof(int) * (size_t)M.nnz, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(val, M.val, sizeof(double) * (size_t)M.nnz, cudaMemcpyHostToDevice, s));
+  }
+  out->rp = rp;
+  out->ci = ci;
+  out->val = val;
+  out->rows = (int)M.rows;
+  out->cols = (int)M.cols;
+  return kOk;
+}
+
+static int check_view(const MatView& M, int in_mem, const char* name) {
+  if (M.rows < 0 || M.cols < 0 || M.nnz < 0 || M.rows >= (1ll << 31) - 1 ||
+      M.cols >= (1ll << 31) - 1 || M.nnz >= (1ll << 31) - 1) {
+    set_error(std::string(name) + ": sizes must be non-negative and below 2^31 - 1");
+    return kErrInvalid;
+  }
+  if (!M.rp || (M.nnz > 0 && (!M.ci || !M.val))) {
+    set_error(std::string(name) + ": null pointer");
+    return kErrInvalid;
+  }
+  if (in_mem == 0) {
+    if (M.rp[M.rows] - M.rp[0] != M.nnz) {
+      set_error(std::string(name) + ": row_ptr[rows] - row_ptr[0] != nnz");
+      return kErrInvalid;
+    }
+  }
+  return kOk;
+}
+
+static int do_transpose(DeviceCtx* ctx, Csr A, long long nnz, Scratch& sc, cudaStream_t s,
+                        Csr* AT, bool detach) {
+  int* trp = sc.get<int>((size_t)A.cols + 1);
+  int* tci = sc.get<int>((size_t)nnz);
+  double* tval = sc.get<double>((size_t)nnz);
+  void* tscr = sc.get<char>(transpose_scratch_bytes(A.rows, A.cols, nnz));
+  if (sc.failed) {
+    set_error("device pool allocation failed for the transpose");
+    return kErrOom;
+  }
+  launch_transpose(A, nnz, trp, tci, tval, tscr, ctx->num_sms, s);
+  note_launches(16);
+  AT->rp = trp;
+  AT->ci = tci;
+  AT->val = tval;
+  AT->rows = A.cols;
+  AT->cols = A.rows;
+  if (detach) {
+    sc.detach(trp);
+    sc.detach(tci);
+    sc.detach(tval);
+  }
+  return kOk;
+}
+
+static bool prof_env() { return env_flag("APPT_PROF"); }
+
+static void print_prof(const char* tag, const CallStats& st) {
+  for (int p = 0; p < 8; ++p)
+    if (st.ms_phase[p] > 0.0) fprintf(stderr, "[%s] %-16s %7.3f ms\n", tag, kPhaseNames[p], st.ms_phase[p]);
+  fprintf(stderr, "[%s] TOTAL(GPU)      %7.3f ms\n", tag, st.ms_total);
+}
+
+// Core call. Returns C in device memory (pool allocations) in *dc.
+static int run(const MatView& A, const MatView* B, const CallOptions& opt, DeviceCtx* ctx,
+               cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* dc, CallStats* st) {
+  int rc = check_view(A, opt.in_mem, "A");
+  if (rc) return rc;
+  const bool ab = opt.op == kOpAB || opt.op == kOpABUpper;
+  if (B && ab) {
+    rc = check_view(*B, opt.in_mem, "B");
+    if (rc) return rc;
+  }
+  Csr dA{}, dB{};
+  tm.begin(kPhH2D);
+  if (opt.in_mem == 0) {
+    rc = stage_operand(A, sc, s, &dA);
+    if (rc) return rc;
+  } else {
+    dA = Csr{A.rp, A.ci, A.val, (int)A.rows, (int)A.cols};
+  }
+  long long b_nnz = A.nnz;
+  if (ab) {
+    if (B) {
+      if (A.cols != B->rows) {
+        set_error("A.cols != B.rows");
+        return kErrInvalid;
+      }
+      b_nnz = B->nnz;
+      if (opt.in_mem == 0) {
+        rc = stage_operand(*B, sc, s, &dB);
+        if (rc) return rc;
+      } else {
+        dB = Csr{B->rp, B->ci, B->val, (int)B->rows, (int)B->cols};
+      }
+    } else {
+      if (A.rows != A.cols) {
+        set_error("C = A*A needs a square A");
+        return kErrInvalid;
+      }
+      dB = dA;
+    }
+  } else {
+    tm.begin(kPhTranspose);
+    rc = do_transpose(ctx, dA, A.nnz, sc, s, &dB, false);
+    if (rc) return rc;
+    b_nnz = A.nnz;
+  }
+  (void)b_nnz;
+  if (A.rows + opt.row_base >= (1ll << 31) || opt.row_base < 0) {
+    set_error("row_base + rows exceeds int32");
+    return kErrInvalid;
+  }
+  const int upper = (opt.op == kOpAATUpper || opt.op == kOpABUpper) ? 1 : 0;
+  return multiply_device(ctx, dA, dB, A.nnz, upper, (int)opt.row_base,
+                         opt.method, s, sc, tm, dc, st);
+}
+
+int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C,
+           CallStats* st) {
+  if (!C) {
+    set_error("null output");
+    return kErrInvalid;
+  }
+  std::memset((void*)C, 0, sizeof(*C));
+  if (opt.op < 0 || opt.op > 3 || opt.method < 0 || opt.method > 3) {
+    set_error("bad op or method");
+    return kErrInvalid;
+  }
+  DeviceCtx* ctx = nullptr;
+  int rc = get_ctx(opt.device, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  CK(cudaSetDevice(opt.device));
+  cudaStream_t s = opt.stream ? (cudaStream_t)opt.stream : ctx->stream;
+  const long long launches0 = kernel_launches();
+  CallStats local;
+  CallStats* stp = st ? st : &local;
+  *stp = CallStats();
+  PhaseTimer tm;
+  tm.start(opt.timing != 0 || prof_env(), s);
+  DevC dc;
+  {
+    Scratch sc(ctx, s);
+    rc = run(A, B, opt, ctx, s, sc, tm, &dc, stp);
+    if (rc == kOk && opt.out_mem == 0) {
+      // host result: pinned allocation owned by the caller (appt_free_out)
+      tm.begin(kPhD2H);
+      const size_t bytes = sizeof(long long) * ((size_t)dc.rows + 1) + sizeof(int) * (size_t)dc.nnz +
+                           sizeof(double) * (size_t)dc.nnz + 64;
+      void* h = nullptr;
+      int kind = 2;
+      if (cudaMallocHost(&h, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        h = std::malloc(bytes);
+        kind = 3;
+      }
+      if (!h) {
+        set_error("host allocation failed for C");
+        rc = kErrOom;
+      } else {
+        char* p = (char*)h;
+        C->rp = (long long*)p;
+        p += sizeof(long long) * ((size_t)dc.rows + 1);
+        C->val = (double*)(((uintptr_t)p + sizeof(int) * (size_t)dc.nnz + 7) & ~(uintptr_t)7);
+        C->ci = (int*)p;
+        cudaMemcpyAsync(C->rp, dc.rp, sizeof(long long) * ((size_t)dc.rows + 1),
+                        cudaMemcpyDeviceToHost, s);
+        if (dc.nnz > 0) {
+          cudaMemcpyAsync(C->ci, dc.ci, sizeof(int) * (size_t)dc.nnz, cudaMemcpyDeviceToHost, s);
+          cudaMemcpyAsync(C->val, dc.val, sizeof(double) * (size_t)dc.nnz, cudaMemcpyDeviceToHost, s);
+        }
+        tm.end();
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) {
+          set_error(std::string("D2H of C: ") + cudaGetErrorString(e));
+          rc = kErrCuda;
+        }
+        C->mem = 0;
+        C->alloc_kind = kind;
+        C->base = h;
+      }
+      cudaFreeAsync(dc.rp, s);
+      cudaFreeAsync(dc.ci, s);
+      cudaFreeAsync(dc.val, s);
+    } else if (rc == kOk) {
+      C->rp = dc.rp;
+      C->ci = dc.ci;
+      C->val = dc.val;
+      C->mem = 1;
+      C->alloc_kind = 1;
+      C->base = (void*)s;   // stream the pool allocations are ordered on
+    } else if (dc.rp) {
+      cudaFreeAsync(dc.rp, s);
+      cudaFreeAsync(dc.ci, s);
+      cudaFreeAsync(dc.val, s);
+    }
+  }
+  tm.finish(stp);
+  stp->launches = kernel_launches() - launches0;
+  if (rc == kOk) {
+    C->rows = dc.rows;
+    C->cols = dc.cols;
+    C->nnz = dc.nnz;
+    C->device = opt.device;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      set_error(std::string("launch error: ") + cudaGetErrorString(e));
+      free_out(C);
+      return kErrCuda;
+    }
+  }
+  if (prof_env() && rc == kOk) print_prof("appt-prof", *stp);
+  return rc;
+}
+
+int free_out(MatOut* C) {
+  if (!C) return kErrInvalid;
+  switch (C->alloc_kind) {
+    case 1:
+      cudaSetDevice(C->device);
+      cudaFreeAsync(C->rp, (cudaStream_t)C->base);
+      cudaFreeAsync(C->ci, (cudaStream_t)C->base);
+      cudaFreeAsync(C->val, (cudaStream_t)C->base);
+      break;
+    case 2:
+      cudaFreeHost(C->base);
+      break;
+    case 3:
+      std::free(C->base);
+      break;
+    case 4:   // separate device allocations (transpose output)
+      cudaSetDevice(C->device);
+      cudaFree(C->rp);
+      cudaFree(C->ci);
+      cudaFree(C->val);
+      break;
+    default:
+      break;
+  }
+  std::memset((void*)C, 0, sizeof(*C));
+  return kOk;
+}
+
+// ------------------------------------------------------------------ transpose / analysis APIs
+int transpose(const MatView& A, const CallOptions& opt, MatOut* AT) {
+  if (!AT) return kErrInvalid;
+  std::memset((void*)AT, 0, sizeof(*AT));
+  int rc = check_view(A, opt.in_mem, "A");
+  if (rc) return rc;
+  DeviceCtx* ctx = nullptr;
+  rc = get_ctx(opt.device, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  CK(cudaSetDevice(opt.device));
+  cudaStream_t s = opt.stream ? (cudaStream_t)opt.stream : ctx->stream;
+  Scratch sc(ctx, s);
+  Csr dA{};
+  if (opt.in_mem == 0) {
+    rc = stage_operand(A, sc, s, &dA);
+    if (rc) return rc;
+  } else {
+    dA = Csr{A.rp, A.ci, A.val, (int)A.rows, (int)A.cols};
+  }
+  Csr T{};
+  rc = do_transpose(ctx, dA, A.nnz, sc, s, &T, true);
+  if (rc) return rc;
+  // widen row pointers to int64 for the output format
+  long long* rp64 = nullptr;
+  CK(cudaMalloc(&rp64, sizeof(long long) * ((size_t)A.cols + 1)));
+  {
+    std::vector<int> tmp;   // small: cols + 1 entries
+    tmp.resize((size_t)A.cols + 1);
+    CK(cudaMemcpyAsync(tmp.data(), T.rp, sizeof(int) * tmp.size(), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    std::vector<long long> t64(tmp.begin(), tmp.end());
+    CK(cudaMemcpy(rp64, t64.data(), sizeof(long long) * t64.size(), cudaMemcpyHostToDevice));
+  }
+  int* ci = nullptr;
+  double* val = nullptr;
+  CK(cudaMalloc(&ci, sizeof(int) * ((size_t)A.nnz + 1)));
+  CK(cudaMalloc(&val, sizeof(double) * ((size_t)A.nnz + 1)));
+  CK(cudaMemcpyAsync(ci, T.ci, sizeof(int) * (size_t)A.nnz, cudaMemcpyDeviceToDevice, s));
+  CK(cudaMemcpyAsync(val, T.val, sizeof(double) * (size_t)A.nnz, cudaMemcpyDeviceToDevice, s));
+  cudaFreeAsync((void*)T.rp, s);
+  cudaFreeAsync((void*)T.ci, s);
+  cudaFreeAsync((void*)T.val, s);
+  CK(cudaStreamSynchronize(s));
+  AT->rows = A.cols;
+  AT->cols = A.rows;
+  AT->nnz = A.nnz;
+  AT->device = opt.device;
+  if (opt.out_mem == 1) {
+    AT->rp = rp64;
+    AT->ci = ci;
+    AT->val = val;
+    AT->mem = 1;
+    AT->alloc_kind = 4;
+    return kOk;
+  }
+  const size_t bytes = sizeof(long long) * ((size_t)A.cols + 1) + (sizeof(int) + sizeof(double)) * (size_t)A.nnz + 16;
+  char* h = (char*)std::malloc(bytes);
+  if (!h) {
+    cudaFree(rp64);
+    cudaFree(ci);
+    cudaFree(val);
+    set_error("host allocation failed");
+    return kErrOom;
+  }
+  AT->rp = (long long*)h;
+  AT->val = (double*)(h + sizeof(long long) * ((size_t)A.cols + 1));
+  AT->ci = (int*)(AT->val + A.nnz);
+  CK(cudaMemcpy(AT->rp, rp64, sizeof(long long) * ((size_t)A.cols + 1), cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(AT->ci, ci, sizeof(int) * (size_t)A.nnz, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(AT->val, val, sizeof(double) * (size_t)A.nnz, cudaMemcpyDeviceToHost));
+  cudaFree(rp64);
+  cudaFree(ci);
+  cudaFree(val);
+  AT->mem = 0;
+  AT->alloc_kind = 3;
+  AT->base = h;
+  return kOk;
+}
+
+int row_products(const MatView& A, const MatView* B, const CallOptions& opt, long long* out) {
+  int rc = check_view(A, opt.in_mem, "A");
+  if (rc) return rc;
+  DeviceCtx* ctx = nullptr;
+  rc = get_ctx(opt.device, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  CK(cudaSetDevice(opt.device));
+  cudaStream_t s = opt.stream ? (cudaStream_t)opt.stream : ctx->stream;
+  Scratch sc(ctx, s);
+  Csr dA{}, dB{};
+  if (opt.in_mem == 0) {
+    rc = stage_operand(A, sc, s, &dA);
+    if (rc) return rc;
+    if (B) {
+      rc = stage_operand(*B, sc, s, &dB);
+      if (rc) return rc;
+    } else {
+      dB = dA;
+    }
+  } else {
+    dA = Csr{A.rp, A.ci, A.val, (int)A.rows, (int)A.cols};
+    dB = B ? Csr{B->rp, B->ci, B->val, (int)B->rows, (int)B->cols} : dA;
+  }
+  const int m = (int)A.rows;
+  long long* flop = sc.get<long long>(m);
+  int* lo = sc.get<int>(m);
+  int* hi = sc.get<int>(m);
+  uint8_t* key = sc.get<uint8_t>(m);
+  int* rn = sc.get<int>(m);
+  AnalyzeStats* gst = sc.get<AnalyzeStats>(1);
+  if (sc.failed) return kErrOom;
+  CK(cudaMemsetAsync(gst, 0, sizeof(AnalyzeStats), s));
+  launch_analyze(dA, dB, 0, 0, kMethodAdaptive, lanes_per_row(A.nnz, A.rows), flop, lo, hi, key,
+                 rn, gst, nullptr, ctx->num_sms, s);
+  note_launches(m > 0 ? 1 : 0);
+  if (m > 0) CK(cudaMemcpyAsync(out, flop, sizeof(long long) * (size_t)m, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  return kOk;
+}
+
+int estimate_row_nnz(const MatView& A, int att, const CallOptions& opt, int* out) {
+  int rc = check_view(A, opt.in_mem, "A");
+  if (rc) return rc;
+  DeviceCtx* ctx = nullptr;
+  rc = get_ctx(opt.device, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  CK(cudaSetDevice(opt.device));
+  cudaStream_t s = opt.stream ? (cudaStream_t)opt.stream : ctx->stream;
+  Scratch sc(ctx, s);
+  Csr dA{}, dB{};
+  if (opt.in_mem == 0) {
+    rc = stage_operand(A, sc, s, &dA);
+    if (rc) return rc;
+  } else {
+    dA = Csr{A.rp, A.ci, A.val, (int)A.rows, (int)A.cols};
+  }
+  if (att) {
+    rc = do_transpose(ctx, dA, A.nnz, sc, s, &dB, false);
+    if (rc) return rc;
+  } else {
+    dB = dA;
+  }
+  const int m = (int)A.rows;
+  int* est = sc.get<int>(m);
+  if (sc.failed) return kErrOom;
+  if (A.nnz < 100000) {
+    launch_flop_count_i32(dA, dB, est, s);
+    note_launches(m > 0 ? 1 : 0);
+  } else {
+    unsigned* sketch = sc.get<unsigned>((size_t)dB.rows * 128);
+    if (sc.failed) return kErrOom;
+    launch_minhash_estimate(dA, dB, sketch, est, ctx->num_sms, s);
+    note_launches(2);
+  }
+  if (m > 0) CK(cudaMemcpyAsync(out, est, sizeof(int) * (size_t)m, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  return kOk;
+}
+
+double reference_score(const int* row_ptr, long long rows, long long nnz) {
+  int max_row = 0;
+  for (long long i = 0; i < rows; ++i) max_row = std::max(max_row, row_ptr[i + 1] - row_ptr[i]);
+  const double avg = rows > 0 ? (double)nnz / (double)rows : 0.0;
+  const double skew = avg > 0.0 ? (double)max_row / avg : 0.0;
+  const double fp = (double)nnz * (double)nnz / (double)std::max<long long>(rows, 1);
+  const double lfp = std::log10(std::max(fp, 1.0));
+  const double ln = std::log10((double)rows);
+  const double lmr = std::log10((double)std::max(max_row, 1));
+  const double lsk = std::log10(std::max(skew, 1.0));
+  return -0.4259 * lfp - 0.4215 * ln - 0.6441 * lmr - 0.6420 * lsk + 5.4297;
+}
+
+// ------------------------------------------------------------------ pools (mempool.h semantics)
+bool g_mempool_on = false;
+bool g_devpool_on = false;
+static char* g_hbase = nullptr;
+static size_t g_hcap = 0, g_hoff = 0;
+static std::vector<std::pair<void*, size_t>> g_dev_live;
+static size_t g_dev_used = 0;
+static std::mutex g_pool_mu;
+
+static size_t env_mb(const char* k, size_t def_mb) {
+  const char* e = std::getenv(k);
+  if (e && *e) {
+    long v = std::atol(e);
+    if (v > 0) return (size_t)v << 20;
+  }
+  return def_mb << 20;
+}
+
+bool pool_init(size_t cap_bytes) {
+  std::lock_guard<std::mutex> g(g_pool_mu);
+  if (!g_mempool_on) return true;
+  if (cap_bytes == 0) cap_bytes = env_mb("MP_HOST_MB", 256);
+  if (g_hbase && g_hcap >= cap_bytes) return true;
+  if (g_hbase) cudaFreeHost(g_hbase);
+  g_hbase = nullptr;
+  g_hcap = g_hoff = 0;
+  if (cudaMallocHost((void**)&g_hbase, cap_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    g_hbase = nullptr;
+    set_error("cudaMallocHost of the pinned arena failed");
+    return false;
+  }
+  g_hcap = cap_bytes;
+  return true;
+}
+
+void pool_destroy() {
+  std::lock_guard<std::mutex> g(g_pool_mu);
+  if (g_hbase) cudaFreeHost(g_hbase);
+  g_hbase = nullptr;
+  g_hcap = g_hoff = 0;
+  for (auto& p : g_dev_live) cudaFreeAsync(p.first, 0);
+  g_dev_live.clear();
+  g_dev_used = 0;
+}
+
+int pinned_alloc_reset(void** out, size_t bytes) {
+  if (!out) return (int)cudaErrorInvalidValue;
+  if (!g_mempool_on) return (int)cudaMallocHost(out, bytes ? bytes : 1);
+  std::lock_guard<std::mutex> g(g_pool_mu);
+  if (bytes == 0) bytes = 1;
+  if (!g_hbase || bytes > g_hcap) {
+    // grow (the previous C is dead by contract: each call resets the arena)
+    size_t cap = std::max(bytes + (bytes >> 3), env_mb("MP_HOST_MB", 256));
+    if (g_hbase) cudaFreeHost(g_hbase);
+    g_hbase = nullptr;
+    g_hcap = 0;
+    cudaError_t e = cudaMallocHost((void**)&g_hbase, cap);
+    if (e != cudaSuccess) {
+      g_hbase = nullptr;
+      return (int)e;
+    }
+    g_hcap = cap;
+  }
+  g_hoff = bytes;
+  *out = g_hbase;
+  return 0;
+}
+
+void pinned_release(void* p) {
+  if (!p) return;
+  if (!g_mempool_on) cudaFreeHost(p);
+}
+
+void host_release(void* p) {
+  if (!p) return;
+  if (g_mempool_on) cudaFreeHost(p);
+  else std::free(p);
+}
+
+void devarena_reset() {
+  std::lock_guard<std::mutex> g(g_pool_mu);
+  if (!g_devpool_on) return;
+  for (auto& p : g_dev_live) cudaFreeAsync(p.first, 0);
+  g_dev_live.clear();
+  g_dev_used = 0;
+}
+
+void* devarena_alloc(size_t bytes) {
+  if (bytes == 0) bytes = 1;
+  if (!g_devpool_on) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("cudaMalloc failed in dev_alloc");
+      return nullptr;
+    }
+    return p;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DeviceCtx* ctx = nullptr;
+  if (get_ctx(dev, &ctx)) return nullptr;
+  void* p = nullptr;
+  if (cudaMallocFromPoolAsync(&p, bytes, ctx->pool, 0) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("device pool allocation failed in dev_alloc");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> g(g_pool_mu);
+  g_dev_live.push_back({p, bytes});
+  g_dev_used += bytes;
+  return p;
+}
+
+void devarena_free(void* p) {
+  if (!p) return;
+  if (!g_devpool_on) cudaFree(p);
+}
+
+size_t host_arena_cap() { return g_hcap; }
+size_t host_arena_used() { return g_hoff; }
+size_t devarena_used() { return g_dev_used; }
+
+// ------------------------------------------------------------------ spgemm.h compatible flow
+static inline size_t align8(size_t x) { return (x + 7) & ~(size_t)7; }
+
+void compat_call(void* A_buffer, int A_rows, int A_cols, int A_nnz, void** C_buffer_out,
+                 int* C_rows, int* C_cols, int* C_nnz, int op, int method, const char* tag,
+                 bool att_quirk_cols) {
+  if (C_buffer_out) *C_buffer_out = nullptr;
+  if (C_nnz) *C_nnz = -1;
+  if (C_rows) *C_rows = A_rows;
+  if (C_cols) *C_cols = (op == kOpAB || att_quirk_cols) ? A_cols : A_rows;
+  if (!A_buffer || !C_buffer_out || !C_rows || !C_cols || !C_nnz || A_rows < 0 || A_nnz < 0) {
+    set_error("invalid argument");
+    return;
+  }
+  if (env_flag("APPT_VERBOSE") && method == kMethodAdaptive) {
+    const double sc = reference_score((const int*)A_buffer, A_rows, A_nnz);
+    fprintf(stderr, "[adapt] n=%d score=%.2f (reference rule: %s)\n", A_rows, sc,
+            sc < 0 ? "hash" : "merge3");
+  }
+  MatView A;
+  A.rows = A_rows;
+  A.cols = A_cols;
+  A.nnz = A_nnz;
+  A.rp = (const int*)A_buffer;
+  A.ci = A.rp + (size_t)A_rows + 1;
+  A.val = (const double*)((const char*)A_buffer + align8((size_t)(A_rows + 1) * 4 + (size_t)A_nnz * 4));
+  CallOptions opt;
+  opt.op = op;
+  opt.method = method;
+  opt.in_mem = 0;
+  opt.out_mem = 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  opt.device = dev;
+  const bool prof = prof_env();
+  opt.timing = prof ? 1 : 0;
+  MatOut Cd;
+  CallStats st;
+  int rc = spgemm(A, nullptr, opt, &Cd, &st);
+  if (rc != kOk) {
+    fprintf(stderr, "[appt] %s failed: %s\n", tag, last_error());
+    return;
+  }
+  if (Cd.nnz > 0x7fffffffll) {
+    set_error("nnz(C) exceeds int32; use appt_spgemm");
+    fprintf(stderr, "[appt] %s: nnz(C)=%lld exceeds int32\n", tag, Cd.nnz);
+    free_out(&Cd);
+    return;
+  }
+  DeviceCtx* ctx = nullptr;
+  if (get_ctx(dev, &ctx)) {
+    free_out(&Cd);
+    return;
+  }
+  cudaStream_t s = (cudaStream_t)Cd.base;
+  const size_t rp_al = align8((size_t)(A_rows + 1) * 4);
+  const size_t ci_al = align8((size_t)Cd.nnz * 4);
+  const size_t total = rp_al + ci_al + (size_t)Cd.nnz * 8;
+  void* buf = nullptr;
+  if (pinned_alloc_reset(&buf, total) != 0 || !buf) {
+    set_error("pinned output allocation failed");
+    free_out(&Cd);
+    return;
+  }
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (prof) {
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, s);
+  }
+  int* rp32 = nullptr;
+  bool ok = cudaMallocFromPoolAsync((void**)&rp32, sizeof(int) * ((size_t)A_rows + 1), ctx->pool, s) ==
+            cudaSuccess;
+  if (ok) {
+    narrow_rowptr(Cd.rp, rp32, (long long)A_rows + 1, s);
+    note_launches(1);
+    ok = cudaMemcpyAsync(buf, rp32, sizeof(int) * ((size_t)A_rows + 1), cudaMemcpyDeviceToHost, s) ==
+         cudaSuccess;
+    if (Cd.nnz > 0) {
+      ok = ok && cudaMemcpyAsync((char*)buf + rp_al, Cd.ci, (size_t)Cd.nnz * 4,
+                                 cudaMemcpyDeviceToHost, s) == cudaSuccess;
+      ok = ok && cudaMemcpyAsync((char*)buf + rp_al + ci_al, Cd.val, (size_t)Cd.nnz * 8,
+                                 cudaMemcpyDeviceToHost, s) == cudaSuccess;
+    }
+    cudaFreeAsync(rp32, s);
+  }
+  if (prof) cudaEventRecord(e1, s);
+  ok = ok && cudaStreamSynchronize(s) == cudaSuccess;
+  if (prof) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    st.ms_phase[kPhD2H] += ms;
+    st.ms_total += ms;
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    print_prof(tag, st);
+  }
+  const long long nnz = Cd.nnz;
+  free_out(&Cd);
+  if (!ok) {
+    cudaGetLastError();
+    set_error("device-to-host copy of C failed");
+    pinned_release(buf);
+    return;
+  }
+  *C_buffer_out = buf;
+  *C_nnz = (int)nnz;
+}
+
+void compat_build_csc(const int* d_row_ptr, const int* d_col_idx, const double* d_val, int A_rows,
+                      int A_nnz, int** col_ptr_out, int** row_idx_out, double** val_out) {
+  if (col_ptr_out) *col_ptr_out = nullptr;
+  if (row_idx_out) *row_idx_out = nullptr;
+  if (val_out) *val_out = nullptr;
+  if (!col_ptr_out || !row_idx_out || !val_out || A_rows < 0 || A_nnz < 0) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DeviceCtx* ctx = nullptr;
+  if (get_ctx(dev, &ctx)) return;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  cudaStream_t s = ctx->stream;
+  int *cp = nullptr, *ri = nullptr;
+  double* v = nullptr;
+  if (cudaMalloc(&cp, sizeof(int) * ((size_t)A_rows + 1)) != cudaSuccess ||
+      cudaMalloc(&ri, sizeof(int) * ((size_t)A_nnz + 1)) != cudaSuccess ||
+      cudaMalloc(&v, sizeof(double) * ((size_t)A_nnz + 1)) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(cp);
+    cudaFree(ri);
+    cudaFree(v);
+    set_error("cudaMalloc failed in build_csc");
+    return;
+  }
+  {
+    Scratch sc(ctx, s);
+    void* tscr = sc.get<char>(transpose_scratch_bytes(A_rows, A_rows, A_nnz));
+    if (sc.failed) {
+      cudaFree(cp);
+      cudaFree(ri);
+      cudaFree(v);
+      set_error("pool allocation failed in build_csc");
+      return;
+    }
+    Csr A{d_row_ptr, d_col_idx, d_val, A_rows, A_rows};
+    launch_transpose(A, A_nnz, cp, ri, v, tscr, ctx->num_sms, s);
+    note_launches(16);
+  }
+  if (cudaStreamSynchronize(s) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(cp);
+    cudaFree(ri);
+    cudaFree(v);
+    set_error("build_csc failed");
+    return;
+  }
+  *col_ptr_out = cp;
+  *row_idx_out = ri;
+  *val_out = v;
+}
+
+bool compat_should_run_method(const char* key) {
+  const char* m = std::getenv("METHOD");
+  if (!m || !*m || !std::strcmp(m, "all")) return true;
+  if (!key) return false;
+  for (int i = 0;; ++i) {
+    char a = m[i], b = key[i];
+    if (a >= 'A' && a <= 'Z') a += 32;
+    if (b >= 'A' && b <= 'Z') b += 32;
+    if (a != b) return false;
+    if (a == 0) return true;
+  }
+}
+
+}  // namespace appt

@@ -1,0 +1,117 @@
+// Host-side launchers for the engine's kernels. Every launcher is asynchronous on `s`.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+#include "common.cuh"
+
+namespace appt {
+
+constexpr int kMaxBins = 16;
+
+// Capacities shared by the classifier and the kernels.
+constexpr int kDenseCols = 1280;        // warp dense-window tier: span <= this many columns
+constexpr int kWindowCols = 16384;      // CTA window tier: columns per window
+constexpr int kHashBlockSlots = 8192;   // CTA hash tier: table slots (rows with nnz <= slots/2)
+constexpr int kSymBlockWords = 32768;   // CTA symbolic bitmap window: 2^20 columns
+constexpr int kMergeMaxLists = 256;     // merge tier: rows with more A entries use other tiers
+
+// ---- symbolic bins (chosen per row from products count and column span) ----
+enum SymBin : int {
+  kSymWarpS = 0,   // warp per row, 256-word smem table (bitmap or key hash)
+  kSymWarpM,       // warp per row, 1024-word table
+  kSymWarpL,       // warp per row, 4096-word table
+  kSymBlock,       // CTA per row, 2^20-column bitmap windows (any row)
+  kNumSymBins      // (index kNumSymBins itself is the merge-count bin of the merge method)
+};
+
+// ---- numeric bins (chosen per row from exact nnz, products count and span) ----
+enum NumBin : int {
+  kNumDense = 0,   // warp per row, dense fp64 window over the row's column span
+  kNumHash64,      // warp per row, hash tables of 64 .. 1024 slots
+  kNumHash128,
+  kNumHash256,
+  kNumHash512,
+  kNumHash1024,
+  kNumHashBlock,   // CTA per row, 8192-slot table
+  kNumWindow,      // CTA per row, dense windows of 16384 columns (heavy rows)
+  kNumMerge,       // warp per row, k-way merge of the row's B rows (merge method)
+  kNumNumBins
+};
+
+// Method selector shared by the C-ABI and the dispatcher.
+enum Method : int {
+  kMethodAdaptive = 0,   // per-bin choice (dense / hash / window)
+  kMethodHash = 1,       // hash tiers only (window tier for rows beyond smem)
+  kMethodMerge = 2,      // k-way merge tier for every row
+  kMethodEsc = 3,        // expand - sort - compress baseline
+};
+
+struct AnalyzeStats {          // device-side global statistics (atomics)
+  unsigned long long total_flop;
+  unsigned long long max_flop;
+  unsigned long long max_span;
+  unsigned long long pad;
+};
+
+// util.cu
+size_t scan_scratch_elems(long long n);
+void scan_exclusive(const int* in, long long* out, long long n, long long* scratch, cudaStream_t s);
+void scan_exclusive(const long long* in, long long* out, long long n, long long* scratch,
+                    cudaStream_t s);
+size_t partition_scratch_bytes(int m, int nb);
+void partition_rows(const uint8_t* key, int m, int nb, int* out_rows, long long* bin_off,
+                    void* scratch, cudaStream_t s);
+void narrow_rowptr(const long long* in, int* out, long long n, cudaStream_t s);
+void iota(int* out, int n, cudaStream_t s);
+
+// analyze.cu
+void launch_analyze(Csr A, Csr B, int upper, int row_base, int method, int lanes_per_row,
+                    long long* flop, int* lo, int* hi, uint8_t* symkey, int* row_nnz,
+                    AnalyzeStats* stats, int* err, int num_sms, cudaStream_t s);
+void launch_classify_numeric(Csr A, int m, int method, const long long* flop, const int* lo,
+                             const int* hi, const int* row_nnz, uint8_t* numkey, int num_sms,
+                             cudaStream_t s);
+
+// symbolic.cu
+void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
+                     int row_base, const int* lo, const int* hi, const long long* flop,
+                     int* row_nnz, int* err, int num_sms, cudaStream_t s);
+
+// numeric.cu
+void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows_host,
+                    Csr A, Csr B, int upper, int row_base, const int* lo, const int* hi,
+                    const long long* crp, int* cci, double* cval, int* err, int num_sms,
+                    cudaStream_t s);
+
+// merge.cu
+void launch_merge_count(const int* rows, const long long* bin_off, int bin, Csr A, Csr B,
+                        int upper, int row_base, int* row_nnz, int* err, int num_sms,
+                        cudaStream_t s);
+void launch_merge_numeric(const int* rows, const long long* bin_off, int bin, long long nrows,
+                          Csr A, Csr B, int upper, int row_base, const long long* crp, int* cci,
+                          double* cval, int* err, int num_sms, cudaStream_t s);
+
+// segsort.cu
+size_t segsort_scratch_bytes(int nseg);
+void segsort(int* keys, double* vals, int* keys_alt, double* vals_alt, const long long* off,
+             int nseg, void* scratch, int num_sms, cudaStream_t s);
+
+// esc_transpose.cu
+void launch_esc_expand(Csr A, Csr B, int upper, int row_base, const long long* foff, int* keys,
+                       double* vals, int num_sms, cudaStream_t s);
+void launch_esc_count(int m, const long long* foff, const int* keys, int* row_nnz, int num_sms,
+                      cudaStream_t s);
+void launch_esc_compress(int m, const long long* foff, const int* keys, const double* vals,
+                         const long long* crp, int* cci, double* cval, int num_sms,
+                         cudaStream_t s);
+size_t transpose_scratch_bytes(int rows, int cols, long long nnz);
+void launch_transpose(Csr A, long long nnz, int* t_rp, int* t_ci, double* t_val, void* scratch,
+                      int num_sms, cudaStream_t s);
+
+// minhash.cu
+void launch_minhash_estimate(Csr A, Csr B, unsigned* sketch, int* est, int num_sms,
+                             cudaStream_t s);
+void launch_flop_count_i32(Csr A, Csr B, int* out, cudaStream_t s);
+
+}  // namespace appt

@@ -1,0 +1,522 @@
+// Numeric phase: accumulate a_ik * b_kj for every row of C and write the row, sorted by column,
+// straight to its final place (row offsets come from the exact symbolic count).
+//
+// Reference counterparts: hash_spa_kernel + hash_ultra_kernel (spgemm_kernel_hash.cu:373-458,
+// 573-608) followed by hash_compact_sort_kernel / hash_compact_copy_kernel (:635-674, 773-786).
+// The reference accumulates into an estimate-sized scratch buffer and sorts/copies it into C in
+// a second pass; here each tier sorts inside shared memory and stores C once.
+//
+// Tiers (bins chosen by the classifier in analyze.cu):
+//   dense   warp per row; fp64 window over the row's span + presence bitmap; the bitmap gives
+//           the sorted order directly (banded and narrow-stencil rows)
+//   hash    warp per row; table of T slots (int key + fp64 value), compaction, warp bitonic sort
+//   hashB   CTA per row; 8192-slot table, block bitonic sort
+//   window  CTA per row; dense windows of 16384 columns walked over the row's span (heavy rows)
+#include <climits>
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace appt {
+
+namespace {
+
+// --------------------------------------------------------------------------- warp hash tier
+template <int T, int WPB>
+__global__ void __launch_bounds__(WPB * 32) num_warp_hash_kernel(
+    const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
+    const long long* crp, int* cci, double* cval, int* err) {
+  extern __shared__ __align__(16) unsigned char num_smem[];
+  constexpr int LG = (T == 64) ? 6 : (T == 128) ? 7 : (T == 256) ? 8 : (T == 512) ? 9 : 10;
+  static_assert((1 << LG) == T, "table size must be a power of two in [64, 1024]");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double* vals = reinterpret_cast<double*>(num_smem) + warp * T;
+  int* keys = reinterpret_cast<int*>(reinterpret_cast<double*>(num_smem) + WPB * T) + warp * T;
+  const long long b0 = bin_off[bin];
+  const long long nrows = bin_off[bin + 1] - b0;
+  for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
+       r += (long long)gridDim.x * WPB) {
+    const int i = rows[b0 + r];
+    const int ig = i + row_base;
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    const long long c0 = crp[i];
+    const int n = (int)(crp[i + 1] - c0);
+    for (int s = lane; s < T; s += 32) {
+      keys[s] = -1;
+      vals[s] = 0.0;
+    }
+    __syncwarp();
+    bool overflow = false;
+    for (int base = rs; base < re; base += 32) {
+      const int p = base + lane;
+      const bool v = p < re;
+      const int k = v ? A.ci[p] : 0;
+      const int bs = v ? B.rp[k] : 0;
+      const int len = v ? B.rp[k + 1] - bs : 0;
+      const double a = v ? A.val[p] : 0.0;
+      const int incl = warp_incl_scan(len);
+      const int excl = incl - len;
+      const int total = __shfl_sync(kFull, incl, 31);
+      for (int t0 = 0; t0 < total; t0 += 32) {
+        const int t = t0 + lane;
+        const int L = warp_owner(excl, t);
+        const int bsL = __shfl_sync(kFull, bs, L), exL = __shfl_sync(kFull, excl, L);
+        const double aL = __shfl_sync(kFull, a, L);
+        if (t < total) {
+          const int q = bsL + t - exL;
+          const int j = B.ci[q];
+          if (upper && j < ig) continue;
+          const double prod = aL * B.val[q];
+          unsigned s = hash_slot((unsigned)j, LG);
+          int probe = 0;
+          for (; probe < T; ++probe) {
+            const int old = atomicCAS(&keys[s], -1, j);
+            if (old == -1 || old == j) {
+              atomicAdd(&vals[s], prod);
+              break;
+            }
+            s = (s + 1) & (T - 1);
+          }
+          if (probe == T) overflow = true;
+        }
+      }
+    }
+    __syncwarp();
+    // compact the occupied slots to the front (reads of a chunk precede its writes)
+    int pos = 0;
+    for (int c = 0; c < T; c += 32) {
+      const int kk = keys[c + lane];
+      const double vv = vals[c + lane];
+      const bool valid = kk >= 0;
+      const unsigned bal = __ballot_sync(kFull, valid);
+      __syncwarp();
+      if (valid) {
+        const int d = pos + __popc(bal & lanemask_lt());
+        keys[d] = kk;
+        vals[d] = vv;
+      }
+      pos += __popc(bal);
+      __syncwarp();
+    }
+    int P2 = 1;
+    while (P2 < pos) P2 <<= 1;
+    for (int x = pos + lane; x < P2; x += 32) keys[x] = INT_MAX;
+    __syncwarp();
+    for (int kk = 2; kk <= P2; kk <<= 1) {
+      for (int jj = kk >> 1; jj > 0; jj >>= 1) {
+        for (int x = lane; x < P2; x += 32) {
+          const int y = x ^ jj;
+          if (y > x) {
+            const int kx = keys[x], ky = keys[y];
+            const bool up = (x & kk) == 0;
+            if ((kx > ky) == up) {
+              keys[x] = ky;
+              keys[y] = kx;
+              const double tv = vals[x];
+              vals[x] = vals[y];
+              vals[y] = tv;
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+    const int nw = pos < n ? pos : n;
+    const bool any_overflow = __any_sync(kFull, overflow);
+    if (lane == 0 && (pos != n || any_overflow)) set_error(err, kErrTableFull);
+    for (int t = lane; t < nw; t += 32) {
+      cci[c0 + t] = keys[t];
+      cval[c0 + t] = vals[t];
+    }
+    __syncwarp();
+  }
+}
+
+// --------------------------------------------------------------------------- warp dense tier
+template <int DC, int WPB>
+__global__ void __launch_bounds__(WPB * 32) num_warp_dense_kernel(
+    const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
+    const int* lo_arr, const int* hi_arr, const long long* crp, int* cci, double* cval, int* err) {
+  extern __shared__ __align__(16) unsigned char num_smem[];
+  constexpr int W = DC / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double* acc = reinterpret_cast<double*>(num_smem) + warp * DC;
+  unsigned* bm = reinterpret_cast<unsigned*>(num_smem + (size_t)WPB * DC * 8) + warp * W;
+  int* wpre = reinterpret_cast<int*>(num_smem + (size_t)WPB * DC * 8 + (size_t)WPB * W * 4) +
+              warp * (W + 1);
+  const long long b0 = bin_off[bin];
+  const long long nrows = bin_off[bin + 1] - b0;
+  for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
+       r += (long long)gridDim.x * WPB) {
+    const int i = rows[b0 + r];
+    const int ig = i + row_base;
+    const int lo = lo_arr[i], hi = hi_arr[i];
+    const int span = hi - lo + 1;
+    if (span > DC) {
+      if (lane == 0) set_error(err, kErrCapacity);
+      continue;
+    }
+    const int words = (span + 31) >> 5;
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    const long long c0 = crp[i];
+    const int n = (int)(crp[i + 1] - c0);
+    for (int s = lane; s < span; s += 32) acc[s] = 0.0;
+    for (int w = lane; w < words; w += 32) bm[w] = 0u;
+    __syncwarp();
+    for (int base = rs; base < re; base += 32) {
+      const int p = base + lane;
+      const bool v = p < re;
+      const int k = v ? A.ci[p] : 0;
+      const int bs = v ? B.rp[k] : 0;
+      const int len = v ? B.rp[k + 1] - bs : 0;
+      const double a = v ? A.val[p] : 0.0;
+      const int incl = warp_incl_scan(len);
+      const int excl = incl - len;
+      const int total = __shfl_sync(kFull, incl, 31);
+      for (int t0 = 0; t0 < total; t0 += 32) {
+        const int t = t0 + lane;
+        const int L = warp_owner(excl, t);
+        const int bsL = __shfl_sync(kFull, bs, L), exL = __shfl_sync(kFull, excl, L);
+        const double aL = __shfl_sync(kFull, a, L);
+        if (t < total) {
+          const int q = bsL + t - exL;
+          const int j = B.ci[q];
+          if (upper && j < ig) continue;
+          const unsigned off = (unsigned)(j - lo);
+          if (off >= (unsigned)span) {   // B row not sorted / outside the span
+            set_error(err, kErrBounds);
+            continue;
+          }
+          atomicAdd(&acc[off], aL * B.val[q]);
+          atomicOr(&bm[off >> 5], 1u << (off & 31));
+        }
+      }
+    }
+    __syncwarp();
+    int running = 0;
+    for (int w0 = 0; w0 < words; w0 += 32) {
+      const int w = w0 + lane;
+      const int c = (w < words) ? __popc(bm[w]) : 0;
+      const int incl = warp_incl_scan(c);
+      if (w < words) wpre[w] = running + incl - c;
+      running += __shfl_sync(kFull, incl, 31);
+    }
+    __syncwarp();
+    const int nw = running < n ? running : n;
+    if (lane == 0 && running != n) set_error(err, kErrCapacity);
+    for (int t = lane; t < nw; t += 32) {
+      const int w = search_le(wpre, words, t);
+      const int off = w * 32 + nth_set_bit(bm[w], t - wpre[w]);
+      cci[c0 + t] = lo + off;
+      cval[c0 + t] = acc[off];
+    }
+    __syncwarp();
+  }
+}
+
+// --------------------------------------------------------------------------- CTA hash tier
+template <int T, int NT>
+__global__ void __launch_bounds__(NT) num_block_hash_kernel(
+    const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
+    const long long* crp, int* cci, double* cval, int* err) {
+  extern __shared__ __align__(16) unsigned char num_smem[];
+  constexpr int LG = (T == 4096) ? 12 : (T == 8192) ? 13 : 14;
+  static_assert((1 << LG) == T, "table size must be 4096, 8192 or 16384");
+  double* vals = reinterpret_cast<double*>(num_smem);                  // [T]
+  double* a_s = vals + T;                                              // [NT]
+  long long* excl_s = reinterpret_cast<long long*>(a_s + NT);          // [NT]
+  int* keys = reinterpret_cast<int*>(excl_s + NT);                     // [T]
+  int* bs_s = keys + T;                                                // [NT]
+  __shared__ long long sbuf[NT / 32 + 1];
+  const int tid = threadIdx.x;
+  const long long b0 = bin_off[bin];
+  const long long nrows = bin_off[bin + 1] - b0;
+  for (long long r = blockIdx.x; r < nrows; r += gridDim.x) {
+    const int i = rows[b0 + r];
+    const int ig = i + row_base;
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    const long long c0 = crp[i];
+    const int n = (int)(crp[i + 1] - c0);
+    for (int s = tid; s < T; s += NT) {
+      keys[s] = -1;
+      vals[s] = 0.0;
+    }
+    bool overflow = false;
+    __syncthreads();
+    for (int base = rs; base < re; base += NT) {
+      const int p = base + tid;
+      int bs = 0, len = 0;
+      double a = 0.0;
+      if (p < re) {
+        const int k = A.ci[p];
+        bs = B.rp[k];
+        len = B.rp[k + 1] - bs;
+        a = A.val[p];
+      }
+      long long total;
+      const long long ex = block_excl_scan_ll<NT>(len, sbuf, &total);
+      excl_s[tid] = ex;
+      bs_s[tid] = bs;
+      a_s[tid] = a;
+      __syncthreads();
+      for (long long t = tid; t < total; t += NT) {
+        const int L = search_le(excl_s, NT, t);
+        const int q = bs_s[L] + (int)(t - excl_s[L]);
+        const int j = B.ci[q];
+        if (upper && j < ig) continue;
+        const double prod = a_s[L] * B.val[q];
+        unsigned s = hash_slot((unsigned)j, LG);
+        int probe = 0;
+        for (; probe < T; ++probe) {
+          const int old = atomicCAS(&keys[s], -1, j);
+          if (old == -1 || old == j) {
+            atomicAdd(&vals[s], prod);
+            break;
+          }
+          s = (s + 1) & (T - 1);
+        }
+        if (probe == T) overflow = true;
+      }
+      __syncthreads();
+    }
+    // compaction
+    long long pos = 0;
+    for (int c = 0; c < T; c += NT) {
+      const int kk = keys[c + tid];
+      const double vv = vals[c + tid];
+      long long tot;
+      const long long d = block_excl_scan_ll<NT>(kk >= 0 ? 1 : 0, sbuf, &tot);
+      if (kk >= 0) {
+        keys[pos + d] = kk;
+        vals[pos + d] = vv;
+      }
+      pos += tot;
+      __syncthreads();
+    }
+    int P2 = 1;
+    while (P2 < pos) P2 <<= 1;
+    for (int x = (int)pos + tid; x < P2; x += NT) keys[x] = INT_MAX;
+    __syncthreads();
+    for (int kk = 2; kk <= P2; kk <<= 1) {
+      for (int jj = kk >> 1; jj > 0; jj >>= 1) {
+        for (int x = tid; x < P2; x += NT) {
+          const int y = x ^ jj;
+          if (y > x) {
+            const int kx = keys[x], ky = keys[y];
+            const bool up = (x & kk) == 0;
+            if ((kx > ky) == up) {
+              keys[x] = ky;
+              keys[y] = kx;
+              const double tv = vals[x];
+              vals[x] = vals[y];
+              vals[y] = tv;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    const int nw = pos < n ? (int)pos : n;
+    if (tid == 0 && pos != n) set_error(err, kErrTableFull);
+    if (overflow) set_error(err, kErrTableFull);
+    for (int t = tid; t < nw; t += NT) {
+      cci[c0 + t] = keys[t];
+      cval[c0 + t] = vals[t];
+    }
+    __syncthreads();
+  }
+}
+
+// --------------------------------------------------------------------------- CTA window tier
+template <int WC, int NT>
+__global__ void __launch_bounds__(NT) num_block_window_kernel(
+    const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
+    const int* lo_arr, const int* hi_arr, const long long* crp, int* cci, double* cval, int* err) {
+  extern __shared__ __align__(16) unsigned char num_smem[];
+  constexpr int W = WC / 32;
+  static_assert(W <= NT, "one bitmap word per thread in the emit scan");
+  double* acc = reinterpret_cast<double*>(num_smem);                   // [WC]
+  double* a_s = acc + WC;                                              // [NT]
+  long long* excl_s = reinterpret_cast<long long*>(a_s + NT);          // [NT]
+  unsigned* bm = reinterpret_cast<unsigned*>(excl_s + NT);             // [W]
+  int* wpre = reinterpret_cast<int*>(bm + W);                          // [W]
+  int* bs_s = wpre + W;                                                // [NT]
+  __shared__ long long sbuf[NT / 32 + 1];
+  const int tid = threadIdx.x;
+  const long long b0 = bin_off[bin];
+  const long long nrows = bin_off[bin + 1] - b0;
+  for (long long r = blockIdx.x; r < nrows; r += gridDim.x) {
+    const int i = rows[b0 + r];
+    const int ig = i + row_base;
+    const int lo = lo_arr[i], hi = hi_arr[i];
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    const long long c0 = crp[i];
+    const long long n = crp[i + 1] - c0;
+    const bool multi = (long long)hi - lo + 1 > WC;
+    long long out = 0;
+    for (long long w0 = lo; w0 <= hi; w0 += WC) {
+      const long long w1 = (w0 + WC < (long long)hi + 1) ? w0 + WC : (long long)hi + 1;
+      const int wspan = (int)(w1 - w0);
+      const int words = (wspan + 31) >> 5;
+      for (int s = tid; s < wspan; s += NT) acc[s] = 0.0;
+      for (int w = tid; w < words; w += NT) bm[w] = 0u;
+      __syncthreads();
+      for (int base = rs; base < re; base += NT) {
+        const int p = base + tid;
+        int bs = 0, be = 0;
+        double a = 0.0;
+        if (p < re) {
+          const int k = A.ci[p];
+          bs = B.rp[k];
+          be = B.rp[k + 1];
+          a = A.val[p];
+          if (multi) {
+            const int s2 = lower_bound_col(B.ci, bs, be, (int)w0);
+            be = lower_bound_col(B.ci, s2, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
+            bs = s2;
+          }
+        }
+        long long total;
+        const long long ex = block_excl_scan_ll<NT>(be - bs, sbuf, &total);
+        excl_s[tid] = ex;
+        bs_s[tid] = bs;
+        a_s[tid] = a;
+        __syncthreads();
+        for (long long t = tid; t < total; t += NT) {
+          const int L = search_le(excl_s, NT, t);
+          const int q = bs_s[L] + (int)(t - excl_s[L]);
+          const int j = B.ci[q];
+          if (upper && j < ig) continue;
+          if (j < w0 || j >= w1) continue;
+          const unsigned off = (unsigned)(j - w0);
+          atomicAdd(&acc[off], a_s[L] * B.val[q]);
+          atomicOr(&bm[off >> 5], 1u << (off & 31));
+        }
+        __syncthreads();
+      }
+      long long cnt_w;
+      const int c = (tid < words) ? __popc(bm[tid]) : 0;
+      const long long wex = block_excl_scan_ll<NT>(c, sbuf, &cnt_w);
+      if (tid < words) wpre[tid] = (int)wex;
+      __syncthreads();
+      for (int t = tid; t < cnt_w; t += NT) {
+        const int w = search_le(wpre, words, t);
+        const int off = w * 32 + nth_set_bit(bm[w], t - wpre[w]);
+        const long long dst = out + t;
+        if (dst < n) {
+          cci[c0 + dst] = (int)(w0 + off);
+          cval[c0 + dst] = acc[off];
+        }
+      }
+      out += cnt_w;
+      __syncthreads();
+    }
+    if (tid == 0 && out != n) set_error(err, kErrCapacity);
+  }
+}
+
+template <typename K>
+int occupancy_grid(K kern, int threads, size_t smem, int num_sms, long long work_items,
+                   int items_per_block) {
+  int occ = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+  if (occ < 1) occ = 1;
+  long long want = (work_items + items_per_block - 1) / items_per_block;
+  long long cap = (long long)num_sms * occ;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  return (int)want;
+}
+
+template <int T, int WPB>
+void run_warp_hash(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
+                   Csr B, int upper, int row_base, const long long* crp, int* cci, double* cval,
+                   int* err, int num_sms, cudaStream_t s) {
+  const size_t smem = (size_t)WPB * T * (sizeof(double) + sizeof(int));
+  auto kern = num_warp_hash_kernel<T, WPB>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  const int grid = occupancy_grid(kern, WPB * 32, smem, num_sms, nrows, WPB);
+  kern<<<grid, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, crp, cci, cval,
+                                    err);
+}
+
+}  // namespace
+
+void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
+                    Csr B, int upper, int row_base, const int* lo, const int* hi,
+                    const long long* crp, int* cci, double* cval, int* err, int num_sms,
+                    cudaStream_t s) {
+  if (nrows <= 0) return;
+  switch (bin) {
+    case kNumHash64:
+      run_warp_hash<64, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, crp, cci, cval, err,
+                           num_sms, s);
+      break;
+    case kNumHash128:
+      run_warp_hash<128, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, crp, cci, cval, err,
+                            num_sms, s);
+      break;
+    case kNumHash256:
+      run_warp_hash<256, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, crp, cci, cval, err,
+                            num_sms, s);
+      break;
+    case kNumHash512:
+      run_warp_hash<512, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, crp, cci, cval, err,
+                            num_sms, s);
+      break;
+    case kNumHash1024:
+      run_warp_hash<1024, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, crp, cci, cval,
+                             err, num_sms, s);
+      break;
+    case kNumDense: {
+      constexpr int WPB = 4;
+      constexpr int W = kDenseCols / 32;
+      const size_t smem = (size_t)WPB * (kDenseCols * sizeof(double) + W * 4 + (W + 1) * 4);
+      auto kern = num_warp_dense_kernel<kDenseCols, WPB>;
+      static bool attr = false;
+      if (!attr) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = true;
+      }
+      const int grid = occupancy_grid(kern, WPB * 32, smem, num_sms, nrows, WPB);
+      kern<<<grid, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, crp,
+                                        cci, cval, err);
+      break;
+    }
+    case kNumHashBlock: {
+      constexpr int NT = 512;
+      const size_t smem = (size_t)kHashBlockSlots * (8 + 4) + (size_t)NT * (8 + 8 + 4);
+      auto kern = num_block_hash_kernel<kHashBlockSlots, NT>;
+      static bool attr = false;
+      if (!attr) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = true;
+      }
+      const int grid = occupancy_grid(kern, NT, smem, num_sms, nrows, 1);
+      kern<<<grid, NT, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, crp, cci, cval, err);
+      break;
+    }
+    case kNumWindow: {
+      constexpr int NT = 512;
+      constexpr int W = kWindowCols / 32;
+      const size_t smem = (size_t)kWindowCols * 8 + (size_t)NT * (8 + 8 + 4) + (size_t)W * 8;
+      auto kern = num_block_window_kernel<kWindowCols, NT>;
+      static bool attr = false;
+      if (!attr) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = true;
+      }
+      const int grid = occupancy_grid(kern, NT, smem, num_sms, nrows, 1);
+      kern<<<grid, NT, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, crp, cci,
+                                  cval, err);
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+}  // namespace appt

@@ -1,0 +1,280 @@
+// Symbolic phase: exact number of distinct output columns of every row of C.
+//
+// Reference counterpart: the per-row distinct count that the reference gets as a side effect of
+// hash accumulation (hash_spa_kernel's `cnt`, spgemm_kernel_hash.cu:373-458) or from
+// bucket_count_kernel (spgemm_merge.cu:531-571). Here it is a separate, insert-only pass so that
+// C can be allocated exactly once and the numeric pass writes every entry to its final place
+// (no estimate-sized scratch buffer and no compaction copy).
+//
+// Two table kinds share one shared-memory budget per warp:
+//   * bitmap over the row's column span [lo, hi]  (one atomicOr per product, new bits counted)
+//   * open-addressing key hash with Fibonacci slots sized to >= 2 x products (never fills)
+// and rows with <= 32 products and <= 32 A entries use warp match in registers (no table).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace appt {
+
+namespace {
+
+template <int WORDS, int WPB>
+__global__ void __launch_bounds__(WPB * 32) sym_warp_kernel(const int* rows, const long long* bin_off,
+                                                            int bin, Csr A, Csr B, int upper,
+                                                            int row_base, const int* lo_arr,
+                                                            const int* hi_arr,
+                                                            const long long* flop_arr,
+                                                            int* row_nnz, int* err) {
+  extern __shared__ unsigned sym_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned* tab = sym_smem + warp * WORDS;
+  const long long b0 = bin_off[bin];
+  const long long nrows = bin_off[bin + 1] - b0;
+  for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
+       r += (long long)gridDim.x * WPB) {
+    const int i = rows[b0 + r];
+    const int ig = i + row_base;
+    const int lo = lo_arr[i], hi = hi_arr[i];
+    const long long f = flop_arr[i];
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    int cnt = 0;
+    if (f <= 32 && re - rs <= 32) {
+      // register path: at most one product per lane
+      const int p = rs + lane;
+      const bool v = p < re;
+      const int k = v ? A.ci[p] : 0;
+      const int bs = v ? B.rp[k] : 0;
+      const int len = v ? B.rp[k + 1] - bs : 0;
+      const int incl = warp_incl_scan(len);
+      const int excl = incl - len;
+      const int total = __shfl_sync(kFull, incl, 31);
+      const int L = warp_owner(excl, lane);
+      const int bsL = __shfl_sync(kFull, bs, L), exL = __shfl_sync(kFull, excl, L);
+      int j = -1;
+      if (lane < total) {
+        j = B.ci[bsL + lane - exL];
+        if (upper && j < ig) j = -1;
+      }
+      const unsigned peers = __match_any_sync(kFull, j);
+      const bool lead = (j >= 0) && (lane == __ffs(peers) - 1);
+      cnt = __popc(__ballot_sync(kFull, lead));
+    } else {
+      const long long span = (long long)hi - lo + 1;
+      const int words_bm = (int)((span + 31) >> 5);
+      const int lg = ilog2_ceil(f * 2 < 32 ? 32 : f * 2);
+      const bool bm_ok = span <= 32ll * WORDS;
+      const bool h_ok = lg <= 30 && (1 << lg) <= WORDS;
+      if (!bm_ok && !h_ok) {
+        if (lane == 0) {
+          set_error(err, kErrCapacity);
+          row_nnz[i] = 0;
+        }
+        continue;
+      }
+      const int hslots = h_ok ? (1 << lg) : 0;
+      const bool bitmap = bm_ok && (!h_ok || words_bm <= 2 * hslots);
+      const int nclear = bitmap ? words_bm : hslots;
+      const unsigned fill = bitmap ? 0u : kEmptyKey;
+      for (int w = lane; w < nclear; w += 32) tab[w] = fill;
+      __syncwarp();
+      bool overflow = false;
+      for (int base = rs; base < re; base += 32) {
+        const int p = base + lane;
+        const bool v = p < re;
+        const int k = v ? A.ci[p] : 0;
+        const int bs = v ? B.rp[k] : 0;
+        const int len = v ? B.rp[k + 1] - bs : 0;
+        const int incl = warp_incl_scan(len);
+        const int excl = incl - len;
+        const int total = __shfl_sync(kFull, incl, 31);
+        for (int t0 = 0; t0 < total; t0 += 32) {
+          const int t = t0 + lane;
+          const int L = warp_owner(excl, t);
+          const int bsL = __shfl_sync(kFull, bs, L), exL = __shfl_sync(kFull, excl, L);
+          if (t < total) {
+            const int j = B.ci[bsL + t - exL];
+            if (upper && j < ig) continue;
+            if (bitmap) {
+              const unsigned off = (unsigned)(j - lo);
+              if (off >= (unsigned)span) {   // B row not sorted / outside the span
+                overflow = true;
+                continue;
+              }
+              const unsigned bit = 1u << (off & 31);
+              const unsigned old = atomicOr(&tab[off >> 5], bit);
+              cnt += (old & bit) ? 0 : 1;
+            } else {
+              unsigned s = hash_slot((unsigned)j, lg);
+              int probe = 0;
+              for (; probe < hslots; ++probe) {
+                const unsigned old = atomicCAS(&tab[s], kEmptyKey, (unsigned)j);
+                if (old == kEmptyKey) { ++cnt; break; }
+                if (old == (unsigned)j) break;
+                s = (s + 1) & (unsigned)(hslots - 1);
+              }
+              if (probe == hslots) overflow = true;
+            }
+          }
+        }
+      }
+      if (__any_sync(kFull, overflow) && lane == 0) set_error(err, kErrTableFull);
+      cnt = warp_sum(cnt);
+      __syncwarp();
+    }
+    if (lane == 0) row_nnz[i] = cnt;
+  }
+}
+
+// CTA per row. Bitmap windows of WB words (32*WB columns) over [lo, hi]; rows whose span exceeds
+// one window restrict every B row to the window by binary search (B rows are sorted).
+template <int NT, int WB>
+__global__ void __launch_bounds__(NT) sym_block_kernel(const int* rows, const long long* bin_off,
+                                                       int bin, Csr A, Csr B, int upper,
+                                                       int row_base, const int* lo_arr,
+                                                       const int* hi_arr, int* row_nnz, int* err) {
+  extern __shared__ unsigned sym_smem[];
+  unsigned* bm = sym_smem;                                   // [WB]
+  long long* excl_s = (long long*)(sym_smem + WB);           // [NT + 1]
+  int* bs_s = (int*)(excl_s + NT + 1);                       // [NT]
+  __shared__ long long wsum[NT / 32 + 1];
+  __shared__ int red[NT / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long long b0 = bin_off[bin];
+  const long long nrows = bin_off[bin + 1] - b0;
+  for (long long r = blockIdx.x; r < nrows; r += gridDim.x) {
+    const int i = rows[b0 + r];
+    const int ig = i + row_base;
+    const int lo = lo_arr[i], hi = hi_arr[i];
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    const long long span = (long long)hi - lo + 1;
+    const bool multi = span > 32ll * WB;
+    int cnt = 0;
+    for (long long w0 = lo; w0 <= hi; w0 += 32ll * WB) {
+      const long long w1 = (w0 + 32ll * WB < (long long)hi + 1) ? w0 + 32ll * WB : (long long)hi + 1;
+      const int nwords = (int)((w1 - w0 + 31) >> 5);
+      for (int w = tid; w < nwords; w += NT) bm[w] = 0u;
+      __syncthreads();
+      for (int base = rs; base < re; base += NT) {
+        const int p = base + tid;
+        int bs = 0, be = 0;
+        if (p < re) {
+          const int k = A.ci[p];
+          bs = B.rp[k];
+          be = B.rp[k + 1];
+          if (multi) {
+            const int s2 = lower_bound_col(B.ci, bs, be, (int)w0);
+            be = lower_bound_col(B.ci, s2, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
+            bs = s2;
+          }
+        }
+        // block exclusive scan of segment lengths (int64)
+        long long len = be - bs;
+        long long incl = len;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          long long y = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += y;
+        }
+        if (lane == 31) wsum[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+          long long x = lane < NT / 32 ? wsum[lane] : 0;
+          long long xi = x;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            long long y = __shfl_up_sync(kFull, xi, o);
+            if (lane >= o) xi += y;
+          }
+          if (lane < NT / 32) wsum[lane] = xi - x;
+          if (lane == NT / 32 - 1) wsum[NT / 32] = xi;
+        }
+        __syncthreads();
+        excl_s[tid] = wsum[warp] + incl - len;
+        bs_s[tid] = bs;
+        const long long total = wsum[NT / 32];
+        __syncthreads();
+        for (long long t = tid; t < total; t += NT) {
+          // owner: largest L with excl_s[L] <= t
+          int lo_i = 0, hi_i = NT - 1;
+          while (lo_i < hi_i) {
+            int mid = (lo_i + hi_i + 1) >> 1;
+            if (excl_s[mid] <= t) lo_i = mid; else hi_i = mid - 1;
+          }
+          const int j = B.ci[bs_s[lo_i] + (int)(t - excl_s[lo_i])];
+          if (upper && j < ig) continue;
+          if (j < w0 || j >= w1) continue;
+          const unsigned off = (unsigned)(j - w0);
+          const unsigned bit = 1u << (off & 31);
+          const unsigned old = atomicOr(&bm[off >> 5], bit);
+          cnt += (old & bit) ? 0 : 1;
+        }
+        __syncthreads();
+      }
+    }
+    cnt = warp_sum(cnt);
+    if (lane == 0) red[warp] = cnt;
+    __syncthreads();
+    if (tid == 0) {
+      int s = 0;
+      for (int w = 0; w < NT / 32; ++w) s += red[w];
+      row_nnz[i] = s;
+    }
+    __syncthreads();
+  }
+  (void)err;
+}
+
+template <int WORDS, int WPB>
+void launch_sym_warp(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
+                     int row_base, const int* lo, const int* hi, const long long* flop,
+                     int* row_nnz, int* err, int num_sms, cudaStream_t s) {
+  const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
+  auto kern = sym_warp_kernel<WORDS, WPB>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_set = true;
+  }
+  int occ = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, WPB * 32, smem);
+  if (occ < 1) occ = 1;
+  kern<<<num_sms * occ, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi,
+                                              flop, row_nnz, err);
+}
+
+}  // namespace
+
+void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
+                     int row_base, const int* lo, const int* hi, const long long* flop,
+                     int* row_nnz, int* err, int num_sms, cudaStream_t s) {
+  switch (bin) {
+    case kSymWarpS:
+      launch_sym_warp<256, 8>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop, row_nnz,
+                              err, num_sms, s);
+      break;
+    case kSymWarpM:
+      launch_sym_warp<1024, 8>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop, row_nnz,
+                               err, num_sms, s);
+      break;
+    case kSymWarpL:
+      launch_sym_warp<4096, 4>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop, row_nnz,
+                               err, num_sms, s);
+      break;
+    case kSymBlock: {
+      constexpr int NT = 512;
+      const size_t smem = (size_t)kSymBlockWords * 4 + (NT + 1) * 8 + NT * 4;
+      auto kern = sym_block_kernel<NT, kSymBlockWords>;
+      static bool attr_set = false;
+      if (!attr_set) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr_set = true;
+      }
+      kern<<<num_sms, NT, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, row_nnz,
+                                     err);
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+}  // namespace appt

@@ -1,0 +1,181 @@
+"""Parity of the CUDA engine (through the C ABI) with the CPU oracle.
+
+Structure (row_ptr, col_idx) must be bit-exact; values within
+|c - c_ref| <= 1e-12 * max(|c_ref|, sum_k |a_ik b_kj|) (conftest.VALUE_RTOL).
+"""
+import numpy as np
+import pytest
+
+from conftest import abs_product, assert_same_structure, assert_values_close
+
+pytestmark = pytest.mark.gpu
+
+import appt_spgemm as ap  # noqa: E402
+import oracle  # noqa: E402
+from appt_spgemm import matrices as M  # noqa: E402
+
+METHODS = ["adaptive", "hash", "merge", "esc"]
+
+
+def check(A, B=None, op="ab", method="adaptive"):
+    C, st = ap.spgemm(A, B, op=op, method=method, return_stats=True)
+    R = oracle.spgemm(A, B, op=op)
+    assert_same_structure(C, R)
+    assert_values_close(C, R, abs_product(A, B, op))
+    assert st["c_nnz"] == R.nnz
+    return C, st
+
+
+@pytest.mark.parametrize("method", METHODS)
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_random_square(method, seed):
+    A = M.random_csr(300, 300, 0.03 + 0.02 * seed, seed, empty_rows=0.1)
+    check(A, method=method)
+
+
+@pytest.mark.parametrize("method", METHODS)
+@pytest.mark.parametrize("op", ["aat", "aat_upper"])
+def test_random_aat(method, op):
+    A = M.random_csr(257, 131, 0.05, 7, empty_rows=0.05)
+    check(A, op=op, method=method)
+
+
+@pytest.mark.parametrize("method", METHODS)
+def test_rectangular_ab(method):
+    A = M.random_csr(200, 150, 0.04, 11)
+    B = M.random_csr(150, 333, 0.03, 12)
+    check(A, B, method=method)
+
+
+@pytest.mark.parametrize("name", list(M.WORKLOADS))
+@pytest.mark.parametrize("method", METHODS)
+def test_workload_families_small(name, method):
+    A = M.make(name, small=True)
+    op = M.WORKLOADS[name][1]
+    check(A, op=op, method=method)
+    if op == "aat":
+        check(A, op="aat_upper", method=method)
+
+
+def _tier_matrix(n=1 << 18, seed=5):
+    """Rows of very different lengths so that every symbolic and numeric tier is used."""
+    rng = np.random.default_rng(seed)
+    lens = np.minimum(rng.zipf(1.6, n), 700).astype(np.int64)
+    lens[:4] = [600, 300, 150, 2000]
+    lens[np.arange(4, n, 97)] = 0
+    rows = []
+    for i in range(n):
+        L = int(lens[i])
+        if L == 0:
+            rows.append(np.zeros(0, np.int64))
+            continue
+        if i % 3 == 0:   # banded rows (dense tier candidates)
+            c = np.unique(np.clip(i + rng.integers(-300, 300, L), 0, n - 1))
+        else:
+            c = np.unique(rng.integers(0, n, L))
+        rows.append(c)
+    rp = np.zeros(n + 1, np.int64)
+    rp[1:] = np.cumsum([len(r) for r in rows])
+    ci = np.concatenate(rows).astype(np.int32)
+    return M.Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))
+
+
+@pytest.fixture(scope="module")
+def tier_matrix():
+    return _tier_matrix()
+
+
+@pytest.mark.parametrize("method", ["adaptive", "hash", "merge"])
+def test_all_tiers(tier_matrix, method):
+    C, st = check(tier_matrix, method=method)
+    used = {k for k, v in st["bin_rows"].items() if v > 0}
+    if method == "adaptive":
+        assert {"dense", "hash64", "hash_block", "window"} <= used, used
+    if method == "merge":
+        assert "merge" in used and "window" in used, used
+
+
+def test_empty_and_degenerate():
+    Z = M.Csr(0, 0, np.zeros(1, np.int32), np.zeros(0, np.int32), np.zeros(0))
+    C = ap.spgemm(Z)
+    assert C.rows == 0 and C.nnz == 0
+    E = M.Csr(50, 50, np.zeros(51, np.int32), np.zeros(0, np.int32), np.zeros(0))
+    for method in METHODS:
+        C = ap.spgemm(E, method=method)
+        assert C.nnz == 0 and C.rows == 50
+    one = M.Csr(1, 1, np.array([0, 1], np.int32), np.array([0], np.int32), np.array([3.0]))
+    C = ap.spgemm(one)
+    assert C.nnz == 1 and C.val[0] == 9.0
+    # a single dense row hitting every column, plus an identity
+    n = 3000
+    rp = np.concatenate([[0, n], n + np.arange(1, n)]).astype(np.int32)
+    ci = np.concatenate([np.arange(n), np.arange(1, n)]).astype(np.int32)
+    D = M.Csr(n, n, rp, ci, np.random.default_rng(0).uniform(-1, 1, ci.size))
+    for method in METHODS:
+        check(D, method=method)
+
+
+def test_cancellation_keeps_structural_zeros():
+    # row 0 = e0 - e1 ; rows 0 and 1 of B identical -> C[0, :] sums to exact zeros
+    A = M.Csr(3, 3, np.array([0, 2, 4, 5], np.int32), np.array([0, 1, 0, 2, 2], np.int32),
+              np.array([1.0, -1.0, 1.0, 1.0, 1.0]))
+    B = M.Csr(3, 3, np.array([0, 2, 4, 5], np.int32), np.array([1, 2, 1, 2, 0], np.int32),
+              np.array([2.0, 3.0, 2.0, 3.0, 1.0]))
+    for method in METHODS:
+        C = ap.spgemm(A, B, method=method)
+        R = oracle.spgemm(A, B)
+        assert_same_structure(C, R)
+        assert C.nnz == R.nnz == 5
+        assert np.array_equal(C.val[:2], [0.0, 0.0])
+
+
+def test_invalid_column_is_an_error_not_a_fault():
+    A = M.Csr(4, 4, np.array([0, 1, 2, 3, 4], np.int32), np.array([0, 9, 2, 3], np.int32),
+              np.ones(4))
+    with pytest.raises(ap.ApptError):
+        ap.spgemm(A)
+    # the context is still usable afterwards
+    check(M.random_csr(64, 64, 0.1, 3))
+
+
+def test_uniform8_full():
+    check(M.uniform8())
+
+
+def test_stencil27_full():
+    check(M.stencil27())
+
+
+def test_banded_quarter_full():
+    check(M.banded(n=1 << 20))
+
+
+def test_transpose_matches_oracle():
+    A = M.zipf_att(rows=1 << 14, cols=1 << 12)
+    T = ap.transpose(A)
+    R = oracle.transpose(A)
+    assert np.array_equal(T.row_ptr, R.row_ptr.astype(np.int64))
+    assert np.array_equal(T.col_idx, R.col_idx)
+    assert np.array_equal(T.val, R.val)
+
+
+def test_row_products_match_oracle():
+    A = M.rmat(scale=14)
+    assert np.array_equal(ap.row_products(A), oracle.row_products(A))
+
+
+@pytest.mark.parametrize("att", [False, True])
+def test_estimator_matches_reference_restatement(att):
+    small = M.random_csr(500, 500, 0.02, 9)                   # nnz < 100000: products count
+    big = M.stencil27(g=24)                                   # nnz >= 100000: MinHash
+    for A in (small, big):
+        e = ap.estimate_row_nnz(A, att=att)
+        r = oracle.estimate_row_nnz(A, att=att)
+        assert e.shape == r.shape
+        assert (e != r).sum() <= max(1, A.rows // 10000), int((e != r).sum())
+
+
+def test_reference_score_matches_restatement():
+    for name in M.WORKLOADS:
+        A = M.make(name, small=True)
+        assert abs(ap.reference_score(A) - oracle.reference_score(A)) < 1e-12
