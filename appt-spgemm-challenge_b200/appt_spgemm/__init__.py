@@ -30,8 +30,8 @@ OPS = {"ab": 0, "aat": 1, "aat_upper": 2, "ab_upper": 3}
 METHODS = {"adaptive": 0, "hash": 1, "merge": 2, "esc": 3}
 MEM_HOST, MEM_DEVICE = 0, 1
 NUM_BINS = 16
-BIN_NAMES = ["dense", "hash64", "hash128", "hash256", "hash512", "hash1024", "hash_block",
-             "window", "merge"]
+BIN_NAMES = ["rank2k", "rank4k", "rank8k", "hash64", "hash128", "hash256", "hash512", "hash1024",
+             "hash_block", "window", "merge"]
 PHASES = ["h2d", "transpose", "analyze", "symbolic", "scan", "numeric", "d2h", "other"]
 
 # Reference entry points exported with C linkage (include/appt_spgemm.h, layer 1).

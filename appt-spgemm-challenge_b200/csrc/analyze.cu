@@ -19,10 +19,16 @@ constexpr int kAnThreads = 256;
 
 __device__ __forceinline__ int sym_bin_of(long long flop, long long span) {
   if (flop == 0 || span <= 0) return 255;
+  const long long W = (span + 31) >> 5;
+  if (W <= 4096 && W <= 8 * flop + 64) {       // bitmap: clearing/counting W words pays off
+    if (W <= 256) return kSymBmS;
+    if (W <= 1024) return kSymBmM;
+    return kSymBmL;
+  }
   if (flop <= (1ll << 26)) {
-    if (span <= 32ll * 256 || 2 * flop <= 256) return kSymWarpS;
-    if (span <= 32ll * 1024 || 2 * flop <= 1024) return kSymWarpM;
-    if (span <= 32ll * 4096 || 2 * flop <= 4096) return kSymWarpL;
+    if (2 * flop <= 256) return kSymHashS;
+    if (2 * flop <= 1024) return kSymHashM;
+    if (2 * flop <= 4096) return kSymHashL;
   }
   return kSymBlock;
 }
@@ -127,7 +133,11 @@ __device__ __forceinline__ int num_bin_of(int method, long long nnz, long long f
   if (nnz == 0) return 255;
   if (method == kMethodMerge && rowlen <= kMergeMaxLists) return kNumMerge;
   if (method == kMethodAdaptive) {
-    if (span <= kDenseCols && span <= 8 * nnz) return kNumDense;
+    const long long W = (span + 31) >> 5;
+    const long long bytes = ((6 * W + 7) & ~7ll) + 8 * nnz;   // bitmap + prefix + accumulator
+    if (bytes <= 2048) return kNumRank2K;
+    if (bytes <= 4096) return kNumRank4K;
+    if (bytes <= 8192) return kNumRank8K;
     if (nnz > 512 && span <= kWindowCols && span <= 4 * nnz) return kNumWindow;
   }
   if (nnz <= 32) return kNumHash64;

@@ -10,7 +10,6 @@ namespace appt {
 constexpr int kMaxBins = 16;
 
 // Capacities shared by the classifier and the kernels.
-constexpr int kDenseCols = 1280;        // warp dense-window tier: span <= this many columns
 constexpr int kWindowCols = 16384;      // CTA window tier: columns per window
 constexpr int kHashBlockSlots = 8192;   // CTA hash tier: table slots (rows with nnz <= slots/2)
 constexpr int kSymBlockWords = 32768;   // CTA symbolic bitmap window: 2^20 columns
@@ -18,17 +17,22 @@ constexpr int kMergeMaxLists = 256;     // merge tier: rows with more A entries 
 
 // ---- symbolic bins (chosen per row from products count and column span) ----
 enum SymBin : int {
-  kSymWarpS = 0,   // warp per row, 256-word smem table (bitmap or key hash)
-  kSymWarpM,       // warp per row, 1024-word table
-  kSymWarpL,       // warp per row, 4096-word table
+  kSymBmS = 0,     // warp per row, bitmap over the span, <= 256 words   (k-sequential)
+  kSymBmM,         //                                      <= 1024 words
+  kSymBmL,         //                                      <= 4096 words
+  kSymHashS,       // warp per row, key hash of 256 / 1024 / 4096 slots (wide spans)
+  kSymHashM,
+  kSymHashL,
   kSymBlock,       // CTA per row, 2^20-column bitmap windows (any row)
   kNumSymBins      // (index kNumSymBins itself is the merge-count bin of the merge method)
 };
 
 // ---- numeric bins (chosen per row from exact nnz, products count and span) ----
 enum NumBin : int {
-  kNumDense = 0,   // warp per row, dense fp64 window over the row's column span
-  kNumHash64,      // warp per row, hash tables of 64 .. 1024 slots
+  kNumRank2K = 0,  // warp per row, bitmap-rank accumulator in 2 / 4 / 8 KB of shared memory
+  kNumRank4K,
+  kNumRank8K,
+  kNumHash64,      // warp per row, hash tables of 64 .. 1024 slots + in-smem sort
   kNumHash128,
   kNumHash256,
   kNumHash512,
@@ -41,7 +45,7 @@ enum NumBin : int {
 
 // Method selector shared by the C-ABI and the dispatcher.
 enum Method : int {
-  kMethodAdaptive = 0,   // per-bin choice (dense / hash / window)
+  kMethodAdaptive = 0,   // per-row choice (rank / hash / window)
   kMethodHash = 1,       // hash tiers only (window tier for rows beyond smem)
   kMethodMerge = 2,      // k-way merge tier for every row
   kMethodEsc = 3,        // expand - sort - compress baseline

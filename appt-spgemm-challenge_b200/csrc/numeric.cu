@@ -7,14 +7,18 @@
 // a second pass; here each tier sorts inside shared memory and stores C once.
 //
 // Tiers (bins chosen by the classifier in analyze.cu):
-//   dense   warp per row; fp64 window over the row's span + presence bitmap; the bitmap gives
-//           the sorted order directly (banded and narrow-stencil rows)
+//   rank    warp per row; bitmap over the row's span + 16-bit popcount prefix gives every
+//           column its output position, values accumulate there directly (no table, no sort)
 //   hash    warp per row; table of T slots (int key + fp64 value), compaction, warp bitonic sort
 //   hashB   CTA per row; 8192-slot table, block bitonic sort
 //   window  CTA per row; dense windows of 16384 columns walked over the row's span (heavy rows)
+// The warp tiers visit products k-sequentially (walk.cuh) and round like the sequential
+// algorithm (no FMA), so their sums are bit-identical to the CPU oracle's; the CTA tiers
+// accumulate with shared-memory atomics (order-dependent rounding, within the tolerance).
 #include <climits>
 #include "common.cuh"
 #include "kernels.cuh"
+#include "walk.cuh"
 
 namespace appt {
 
@@ -46,40 +50,21 @@ __global__ void __launch_bounds__(WPB * 32) num_warp_hash_kernel(
     }
     __syncwarp();
     bool overflow = false;
-    for (int base = rs; base < re; base += 32) {
-      const int p = base + lane;
-      const bool v = p < re;
-      const int k = v ? A.ci[p] : 0;
-      const int bs = v ? B.rp[k] : 0;
-      const int len = v ? B.rp[k + 1] - bs : 0;
-      const double a = v ? A.val[p] : 0.0;
-      const int incl = warp_incl_scan(len);
-      const int excl = incl - len;
-      const int total = __shfl_sync(kFull, incl, 31);
-      for (int t0 = 0; t0 < total; t0 += 32) {
-        const int t = t0 + lane;
-        const int L = warp_owner(excl, t);
-        const int bsL = __shfl_sync(kFull, bs, L), exL = __shfl_sync(kFull, excl, L);
-        const double aL = __shfl_sync(kFull, a, L);
-        if (t < total) {
-          const int q = bsL + t - exL;
-          const int j = B.ci[q];
-          if (upper && j < ig) continue;
-          const double prod = aL * B.val[q];
-          unsigned s = hash_slot((unsigned)j, LG);
-          int probe = 0;
-          for (; probe < T; ++probe) {
-            const int old = atomicCAS(&keys[s], -1, j);
-            if (old == -1 || old == j) {
-              atomicAdd(&vals[s], prod);
-              break;
-            }
-            s = (s + 1) & (T - 1);
-          }
-          if (probe == T) overflow = true;
+    walk_row_k_sequential<true>(A, B, rs, re, [&](int j, double x, double a) {
+      if (upper && j < ig) return;
+      unsigned s = hash_slot((unsigned)j, LG);
+      int probe = 0;
+      for (; probe < T; ++probe) {
+        const int old = atomicCAS(&keys[s], -1, j);
+        if (old == -1 || old == j) {
+          // one lane per column in a step: a plain update, ordered across steps by the walk
+          vals[s] = mul_add_rn(vals[s], a, x);
+          break;
         }
+        s = (s + 1) & (T - 1);
       }
-    }
+      if (probe == T) overflow = true;
+    });
     __syncwarp();
     // compact the occupied slots to the front (reads of a chunk precede its writes)
     int pos = 0;
@@ -131,84 +116,88 @@ __global__ void __launch_bounds__(WPB * 32) num_warp_hash_kernel(
   }
 }
 
-// --------------------------------------------------------------------------- warp dense tier
-template <int DC, int WPB>
-__global__ void __launch_bounds__(WPB * 32) num_warp_dense_kernel(
+// --------------------------------------------------------------------------- warp rank tier
+// Row layout in the warp's shared budget: bitmap over [lo, hi] (W words), 16-bit exclusive
+// popcount prefix per word (W entries), fp64 accumulator of nnz entries. The bitmap is rebuilt
+// from the products, after which the output position of column j is
+// prefix[w] + popc(bitmap[w] & below(j)) -- so values accumulate directly into output order and
+// the row needs neither a hash table nor a sort. Products are visited k-sequentially (walk.cuh):
+// no atomics on the accumulator, and each sum is formed in the reference's order.
+template <int BUDGET, int WPB>
+__global__ void __launch_bounds__(WPB * 32) num_warp_rank_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
     const int* lo_arr, const int* hi_arr, const long long* crp, int* cci, double* cval, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
-  constexpr int W = DC / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  double* acc = reinterpret_cast<double*>(num_smem) + warp * DC;
-  unsigned* bm = reinterpret_cast<unsigned*>(num_smem + (size_t)WPB * DC * 8) + warp * W;
-  int* wpre = reinterpret_cast<int*>(num_smem + (size_t)WPB * DC * 8 + (size_t)WPB * W * 4) +
-              warp * (W + 1);
+  unsigned char* base = num_smem + (size_t)warp * BUDGET;
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
   for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
        r += (long long)gridDim.x * WPB) {
     const int i = rows[b0 + r];
     const int ig = i + row_base;
-    const int lo = lo_arr[i], hi = hi_arr[i];
-    const int span = hi - lo + 1;
-    if (span > DC) {
-      if (lane == 0) set_error(err, kErrCapacity);
-      continue;
-    }
-    const int words = (span + 31) >> 5;
+    const int lo = lo_arr[i];
+    const long long span = (long long)hi_arr[i] - lo + 1;
     const int rs = A.rp[i], re = A.rp[i + 1];
     const long long c0 = crp[i];
     const int n = (int)(crp[i + 1] - c0);
-    for (int s = lane; s < span; s += 32) acc[s] = 0.0;
-    for (int w = lane; w < words; w += 32) bm[w] = 0u;
-    __syncwarp();
-    for (int base = rs; base < re; base += 32) {
-      const int p = base + lane;
-      const bool v = p < re;
-      const int k = v ? A.ci[p] : 0;
-      const int bs = v ? B.rp[k] : 0;
-      const int len = v ? B.rp[k + 1] - bs : 0;
-      const double a = v ? A.val[p] : 0.0;
-      const int incl = warp_incl_scan(len);
-      const int excl = incl - len;
-      const int total = __shfl_sync(kFull, incl, 31);
-      for (int t0 = 0; t0 < total; t0 += 32) {
-        const int t = t0 + lane;
-        const int L = warp_owner(excl, t);
-        const int bsL = __shfl_sync(kFull, bs, L), exL = __shfl_sync(kFull, excl, L);
-        const double aL = __shfl_sync(kFull, a, L);
-        if (t < total) {
-          const int q = bsL + t - exL;
-          const int j = B.ci[q];
-          if (upper && j < ig) continue;
-          const unsigned off = (unsigned)(j - lo);
-          if (off >= (unsigned)span) {   // B row not sorted / outside the span
-            set_error(err, kErrBounds);
-            continue;
-          }
-          atomicAdd(&acc[off], aL * B.val[q]);
-          atomicOr(&bm[off >> 5], 1u << (off & 31));
-        }
-      }
+    const int W = (int)((span + 31) >> 5);
+    const int acc_off = ((6 * W) + 7) & ~7;
+    if (span <= 0 || acc_off + 8 * n > BUDGET || n > 65535) {
+      if (lane == 0) set_error(err, kErrCapacity);
+      continue;
     }
+    unsigned* bm = reinterpret_cast<unsigned*>(base);
+    unsigned short* pre = reinterpret_cast<unsigned short*>(base + 4 * W);
+    double* acc = reinterpret_cast<double*>(base + acc_off);
+    for (int w = lane; w < W; w += 32) bm[w] = 0u;
+    for (int t = lane; t < n; t += 32) acc[t] = 0.0;
     __syncwarp();
+    bool bad = false;
+    // 1) presence bitmap of the row's columns
+    walk_row_k_sequential<false>(A, B, rs, re, [&](int j, double, double) {
+      if (upper && j < ig) return;
+      const unsigned off = (unsigned)(j - lo);
+      if (off >= (unsigned)span) {
+        bad = true;
+        return;
+      }
+      atomicOr(&bm[off >> 5], 1u << (off & 31));
+    });
+    // 2) exclusive popcount prefix per word
     int running = 0;
-    for (int w0 = 0; w0 < words; w0 += 32) {
+    for (int w0 = 0; w0 < W; w0 += 32) {
       const int w = w0 + lane;
-      const int c = (w < words) ? __popc(bm[w]) : 0;
+      const int c = (w < W) ? __popc(bm[w]) : 0;
       const int incl = warp_incl_scan(c);
-      if (w < words) wpre[w] = running + incl - c;
+      if (w < W) pre[w] = (unsigned short)(running + incl - c);
       running += __shfl_sync(kFull, incl, 31);
     }
     __syncwarp();
-    const int nw = running < n ? running : n;
-    if (lane == 0 && running != n) set_error(err, kErrCapacity);
-    for (int t = lane; t < nw; t += 32) {
-      const int w = search_le(wpre, words, t);
-      const int off = w * 32 + nth_set_bit(bm[w], t - wpre[w]);
-      cci[c0 + t] = lo + off;
-      cval[c0 + t] = acc[off];
+    if (running != n) bad = true;
+    // 3) accumulate at the column's rank, k by k
+    if (running == n) {
+      walk_row_k_sequential<true>(A, B, rs, re, [&](int j, double x, double a) {
+        if (upper && j < ig) return;
+        const unsigned off = (unsigned)(j - lo);
+        if (off >= (unsigned)span) return;
+        const unsigned w = off >> 5;
+        const int pos = pre[w] + __popc(bm[w] & ((1u << (off & 31)) - 1u));
+        acc[pos] = mul_add_rn(acc[pos], a, x);
+      });
+      // 4) ordered output: t-th set bit of the bitmap and its sum
+      for (int t = lane; t < n; t += 32) {
+        int lo_w = 0, hi_w = W - 1;
+        while (lo_w < hi_w) {
+          const int mid = (lo_w + hi_w + 1) >> 1;
+          if ((int)pre[mid] <= t) lo_w = mid; else hi_w = mid - 1;
+        }
+        const int off = lo_w * 32 + nth_set_bit(bm[lo_w], t - pre[lo_w]);
+        cci[c0 + t] = lo + off;
+        cval[c0 + t] = acc[t];
+      }
     }
+    if (__any_sync(kFull, bad) && lane == 0) set_error(err, kErrCapacity);
     __syncwarp();
   }
 }
@@ -443,6 +432,23 @@ void run_warp_hash(int bin, const int* rows, const long long* bin_off, long long
                                     err);
 }
 
+template <int BUDGET, int WPB>
+void run_warp_rank(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
+                   Csr B, int upper, int row_base, const int* lo, const int* hi,
+                   const long long* crp, int* cci, double* cval, int* err, int num_sms,
+                   cudaStream_t s) {
+  const size_t smem = (size_t)WPB * BUDGET;
+  auto kern = num_warp_rank_kernel<BUDGET, WPB>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  const int grid = occupancy_grid(kern, WPB * 32, smem, num_sms, nrows, WPB);
+  kern<<<grid, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, crp, cci,
+                                    cval, err);
+}
+
 }  // namespace
 
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
@@ -471,21 +477,18 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
       run_warp_hash<1024, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, crp, cci, cval,
                              err, num_sms, s);
       break;
-    case kNumDense: {
-      constexpr int WPB = 4;
-      constexpr int W = kDenseCols / 32;
-      const size_t smem = (size_t)WPB * (kDenseCols * sizeof(double) + W * 4 + (W + 1) * 4);
-      auto kern = num_warp_dense_kernel<kDenseCols, WPB>;
-      static bool attr = false;
-      if (!attr) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-      }
-      const int grid = occupancy_grid(kern, WPB * 32, smem, num_sms, nrows, WPB);
-      kern<<<grid, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, crp,
-                                        cci, cval, err);
+    case kNumRank2K:
+      run_warp_rank<2048, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
+                             cval, err, num_sms, s);
       break;
-    }
+    case kNumRank4K:
+      run_warp_rank<4096, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
+                             cval, err, num_sms, s);
+      break;
+    case kNumRank8K:
+      run_warp_rank<8192, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
+                             cval, err, num_sms, s);
+      break;
     case kNumHashBlock: {
       constexpr int NT = 512;
       const size_t smem = (size_t)kHashBlockSlots * (8 + 4) + (size_t)NT * (8 + 8 + 4);

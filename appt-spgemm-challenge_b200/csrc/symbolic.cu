@@ -12,6 +12,7 @@
 // and rows with <= 32 products and <= 32 A entries use warp match in registers (no table).
 #include "common.cuh"
 #include "kernels.cuh"
+#include "walk.cuh"
 
 namespace appt {
 
@@ -122,6 +123,70 @@ __global__ void __launch_bounds__(WPB * 32) sym_warp_kernel(const int* rows, con
     }
     if (lane == 0) row_nnz[i] = cnt;
   }
+}
+
+// Warp per row, bitmap over [lo, hi] (at most WORDS words), filled k-sequentially with
+// fire-and-forget atomicOr (no return value needed), then counted with one popcount pass.
+template <int WORDS, int WPB>
+__global__ void __launch_bounds__(WPB * 32) sym_warp_bitmap_kernel(
+    const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
+    const int* lo_arr, const int* hi_arr, int* row_nnz, int* err) {
+  extern __shared__ unsigned sym_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned* bm = sym_smem + warp * WORDS;
+  const long long b0 = bin_off[bin];
+  const long long nrows = bin_off[bin + 1] - b0;
+  for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
+       r += (long long)gridDim.x * WPB) {
+    const int i = rows[b0 + r];
+    const int ig = i + row_base;
+    const int lo = lo_arr[i];
+    const long long span = (long long)hi_arr[i] - lo + 1;
+    const int W = (int)((span + 31) >> 5);
+    if (span <= 0 || W > WORDS) {
+      if (lane == 0) {
+        set_error(err, kErrCapacity);
+        row_nnz[i] = 0;
+      }
+      continue;
+    }
+    for (int w = lane; w < W; w += 32) bm[w] = 0u;
+    __syncwarp();
+    bool bad = false;
+    walk_row_k_sequential<false>(A, B, A.rp[i], A.rp[i + 1], [&](int j, double, double) {
+      if (upper && j < ig) return;
+      const unsigned off = (unsigned)(j - lo);
+      if (off >= (unsigned)span) {
+        bad = true;
+        return;
+      }
+      atomicOr(&bm[off >> 5], 1u << (off & 31));
+    });
+    int cnt = 0;
+    for (int w = lane; w < W; w += 32) cnt += __popc(bm[w]);
+    cnt = warp_sum(cnt);
+    if (__any_sync(kFull, bad) && lane == 0) set_error(err, kErrCapacity);
+    if (lane == 0) row_nnz[i] = cnt;
+    __syncwarp();
+  }
+}
+
+template <int WORDS, int WPB>
+void launch_sym_bitmap(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
+                       int row_base, const int* lo, const int* hi, int* row_nnz, int* err,
+                       int num_sms, cudaStream_t s) {
+  const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
+  auto kern = sym_warp_bitmap_kernel<WORDS, WPB>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_set = true;
+  }
+  int occ = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, WPB * 32, smem);
+  if (occ < 1) occ = 1;
+  kern<<<num_sms * occ, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi,
+                                              row_nnz, err);
 }
 
 // CTA per row. Bitmap windows of WB words (32*WB columns) over [lo, hi]; rows whose span exceeds
@@ -247,15 +312,27 @@ void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, 
                      int row_base, const int* lo, const int* hi, const long long* flop,
                      int* row_nnz, int* err, int num_sms, cudaStream_t s) {
   switch (bin) {
-    case kSymWarpS:
+    case kSymBmS:
+      launch_sym_bitmap<256, 8>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz, err,
+                                num_sms, s);
+      break;
+    case kSymBmM:
+      launch_sym_bitmap<1024, 8>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz, err,
+                                 num_sms, s);
+      break;
+    case kSymBmL:
+      launch_sym_bitmap<4096, 4>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz, err,
+                                 num_sms, s);
+      break;
+    case kSymHashS:
       launch_sym_warp<256, 8>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop, row_nnz,
                               err, num_sms, s);
       break;
-    case kSymWarpM:
+    case kSymHashM:
       launch_sym_warp<1024, 8>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop, row_nnz,
                                err, num_sms, s);
       break;
-    case kSymWarpL:
+    case kSymHashL:
       launch_sym_warp<4096, 4>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop, row_nnz,
                                err, num_sms, s);
       break;

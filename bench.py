@@ -184,7 +184,7 @@ def run_reference(args, rank: int, world: int):
                               "unavailable": f"reference build exited {r.returncode}: "
                                              f"{r.stderr.strip().splitlines()[-1:]}"}))
             return 0
-        res = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1])
+        res = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{\"products\"")][-1])
         ms = float(np.mean(res["ms"]))
         val = 2.0 * res["products"] / (ms * 1e-3) / 1e9
         line.update({"value": val, "ms_per_step": ms, "clocks": clocks,

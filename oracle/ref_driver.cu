@@ -110,6 +110,7 @@ int main(int argc, char** argv) {
   cudaSetDevice(0);
   void* A = nullptr;
   int rows = 0, cols = 0, nnz = 0;
+  std::string json;   // printed once at the end: the reference prints its own lines to stdout
   if (!read_bin(in, &A, &rows, &cols, &nnz, mempool)) {
     std::fprintf(stderr, "cannot read %s\n", in);
     return 3;
@@ -131,7 +132,7 @@ int main(int argc, char** argv) {
       std::fprintf(stderr, "mempool_init failed\n");
       return 4;
     }
-    std::printf("{\"products\": %lld", prod);
+    json = "{\"products\": " + std::to_string(prod);
   }
   void* C = nullptr;
   int cr = 0, cc = 0, cn = 0;
@@ -140,16 +141,25 @@ int main(int argc, char** argv) {
     fn(A, rows, cols, nnz, &C, &cr, &cc, &cn);
     if (C) pinned_free(C);
   }
-  std::printf(", \"ms\": [");
+  json += ", \"ms\": [";
   for (int r = 0; r < repeat; ++r) {
     C = nullptr;
     auto t0 = std::chrono::steady_clock::now();
     fn(A, rows, cols, nnz, &C, &cr, &cc, &cn);
     auto t1 = std::chrono::steady_clock::now();
-    std::printf("%s%.6f", r ? ", " : "", std::chrono::duration<double, std::milli>(t1 - t0).count());
+    char buf[64];
+    std::snprintf(buf, sizeof(buf), "%s%.6f", r ? ", " : "",
+                  std::chrono::duration<double, std::milli>(t1 - t0).count());
+    json += buf;
     if (r + 1 < repeat && C) pinned_free(C);
   }
-  std::printf("], \"c_rows\": %d, \"c_cols\": %d, \"c_nnz\": %d}\n", cr, cc, cn);
+  {
+    char buf[160];
+    std::snprintf(buf, sizeof(buf), "], \"c_rows\": %d, \"c_cols\": %d, \"c_nnz\": %d}", cr, cc, cn);
+    json += buf;
+  }
+  std::fflush(stdout);
+  std::printf("\n%s\n", json.c_str());
   std::fflush(stdout);
   if (out && C && cn >= 0) write_bin(out, C, cr, cc, cn);
   if (C) pinned_free(C);

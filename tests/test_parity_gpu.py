@@ -90,9 +90,23 @@ def test_all_tiers(tier_matrix, method):
     C, st = check(tier_matrix, method=method)
     used = {k for k, v in st["bin_rows"].items() if v > 0}
     if method == "adaptive":
-        assert {"dense", "hash64", "hash_block", "window"} <= used, used
+        assert {"rank2k", "hash64", "hash_block", "window"} <= used, used
     if method == "merge":
         assert "merge" in used and "window" in used, used
+
+
+@pytest.mark.parametrize("method", ["adaptive", "hash", "esc"])
+@pytest.mark.parametrize("name", ["uniform8", "stencil27", "banded", "rmat"])
+def test_sequential_tiers_are_bit_exact(name, method):
+    """The warp tiers (rank, warp hash) and ESC sum each column in the reference's k-then-j
+    order with separate multiply and add roundings, so their values equal the oracle's bit for
+    bit (the CTA tiers, used only for rows beyond 512 entries, accumulate with atomics)."""
+    A = M.make(name, small=True)
+    C, st = ap.spgemm(A, method=method, return_stats=True)
+    assert st["bin_rows"]["hash_block"] == 0 and st["bin_rows"]["window"] == 0
+    R = oracle.spgemm(A)
+    assert_same_structure(C, R)
+    assert np.array_equal(C.val, R.val)
 
 
 def test_empty_and_degenerate():
@@ -116,7 +130,8 @@ def test_empty_and_degenerate():
 
 
 def test_cancellation_keeps_structural_zeros():
-    # row 0 = e0 - e1 ; rows 0 and 1 of B identical -> C[0, :] sums to exact zeros
+    # row 0 of A = e0 - e1 and rows 0, 1 of B are equal -> row 0 of C sums to exact zeros,
+    # which stay stored; row 1 of A = e0 + e2 reaches columns {1, 2} u {0}.
     A = M.Csr(3, 3, np.array([0, 2, 4, 5], np.int32), np.array([0, 1, 0, 2, 2], np.int32),
               np.array([1.0, -1.0, 1.0, 1.0, 1.0]))
     B = M.Csr(3, 3, np.array([0, 2, 4, 5], np.int32), np.array([1, 2, 1, 2, 0], np.int32),
@@ -125,8 +140,10 @@ def test_cancellation_keeps_structural_zeros():
         C = ap.spgemm(A, B, method=method)
         R = oracle.spgemm(A, B)
         assert_same_structure(C, R)
-        assert C.nnz == R.nnz == 5
+        assert C.nnz == R.nnz == 6
+        assert np.array_equal(C.row_ptr, [0, 2, 5, 6])
         assert np.array_equal(C.val[:2], [0.0, 0.0])
+        assert np.array_equal(C.val[2:], [1.0, 2.0, 3.0, 1.0])
 
 
 def test_invalid_column_is_an_error_not_a_fault():
