@@ -133,11 +133,11 @@ __device__ __forceinline__ int num_bin_of(int method, long long nnz, long long f
   if (nnz == 0) return 255;
   if (method == kMethodMerge && rowlen <= kMergeMaxLists) return kNumMerge;
   if (method == kMethodAdaptive) {
-    const long long W = (span + 31) >> 5;
-    const long long bytes = ((6 * W + 7) & ~7ll) + 8 * nnz;   // bitmap + prefix + accumulator
-    if (bytes <= 2048) return kNumRank2K;
-    if (bytes <= 4096) return kNumRank4K;
-    if (bytes <= 8192) return kNumRank8K;
+    const long long W = (span + 63) >> 6;
+    const long long bytes = ((10 * W + 7) & ~7ll) + 12 * nnz;  // bitmap, prefix, sums, columns
+    if (bytes <= 2304) return kNumRank2K;
+    if (bytes <= 4608) return kNumRank4K;
+    if (bytes <= 9216) return kNumRank8K;
     if (nnz > 512 && span <= kWindowCols && span <= 4 * nnz) return kNumWindow;
   }
   if (nnz <= 32) return kNumHash64;

@@ -149,6 +149,13 @@ __device__ __forceinline__ int nth_set_bit(unsigned m, int r) {
   return pos;
 }
 
+// Index (0-based) of the r-th set bit of a 64-bit word (r < popcll(m)).
+__device__ __forceinline__ int nth_set_bit64(unsigned long long m, int r) {
+  const unsigned lo = (unsigned)m;
+  const int c = __popc(lo);
+  return r < c ? nth_set_bit(lo, r) : 32 + nth_set_bit((unsigned)(m >> 32), r - c);
+}
+
 // Largest index L in [0, n) with a[L] <= t for a non-decreasing array.
 template <typename T>
 __device__ __forceinline__ int search_le(const T* a, int n, long long t) {

@@ -26,7 +26,7 @@ namespace {
 
 // --------------------------------------------------------------------------- warp hash tier
 template <int T, int WPB>
-__global__ void __launch_bounds__(WPB * 32) num_warp_hash_kernel(
+__global__ void __launch_bounds__(WPB * 32, 2048 / (WPB * 32) * 3 / 4) num_warp_hash_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
     const long long* crp, int* cci, double* cval, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
@@ -117,14 +117,16 @@ __global__ void __launch_bounds__(WPB * 32) num_warp_hash_kernel(
 }
 
 // --------------------------------------------------------------------------- warp rank tier
-// Row layout in the warp's shared budget: bitmap over [lo, hi] (W words), 16-bit exclusive
-// popcount prefix per word (W entries), fp64 accumulator of nnz entries. The bitmap is rebuilt
-// from the products, after which the output position of column j is
-// prefix[w] + popc(bitmap[w] & below(j)) -- so values accumulate directly into output order and
-// the row needs neither a hash table nor a sort. Products are visited k-sequentially (walk.cuh):
-// no atomics on the accumulator, and each sum is formed in the reference's order.
+// Row layout in the warp's shared budget: bitmap over [lo, hi] in 64-bit words (W words), a
+// 16-bit exclusive popcount prefix per word, the fp64 accumulator of the row's nnz entries and
+// the column of every rank (so the finished row is copied out coalesced).
+// The bitmap is rebuilt from the products, after which the output position of column j is
+// prefix[w] + popcount(bitmap[w] & below(j)) -- values accumulate directly in output order, so
+// the row needs neither a hash table nor a sort. Products are visited k-sequentially
+// (walk.cuh): no atomics on the accumulator, and every sum forms in the reference's order.
 template <int BUDGET, int WPB>
-__global__ void __launch_bounds__(WPB * 32) num_warp_rank_kernel(
+__global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? 6 : 7)
+    num_warp_rank_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
     const int* lo_arr, const int* hi_arr, const long long* crp, int* cci, double* cval, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
@@ -141,20 +143,22 @@ __global__ void __launch_bounds__(WPB * 32) num_warp_rank_kernel(
     const int rs = A.rp[i], re = A.rp[i + 1];
     const long long c0 = crp[i];
     const int n = (int)(crp[i + 1] - c0);
-    const int W = (int)((span + 31) >> 5);
-    const int acc_off = ((6 * W) + 7) & ~7;
-    if (span <= 0 || acc_off + 8 * n > BUDGET || n > 65535) {
+    const int W = (int)((span + 63) >> 6);
+    const int acc_off = ((10 * W) + 7) & ~7;
+    if (span <= 0 || acc_off + 12 * n > BUDGET || n > 65535) {
       if (lane == 0) set_error(err, kErrCapacity);
       continue;
     }
-    unsigned* bm = reinterpret_cast<unsigned*>(base);
-    unsigned short* pre = reinterpret_cast<unsigned short*>(base + 4 * W);
+    unsigned long long* bm = reinterpret_cast<unsigned long long*>(base);
+    unsigned* bm32 = reinterpret_cast<unsigned*>(base);              // same bits, 32-bit view
+    unsigned short* pre = reinterpret_cast<unsigned short*>(base + 8 * W);
     double* acc = reinterpret_cast<double*>(base + acc_off);
-    for (int w = lane; w < W; w += 32) bm[w] = 0u;
+    int* col = reinterpret_cast<int*>(base + acc_off + 8 * n);
+    for (int w = lane; w < W; w += 32) bm[w] = 0ull;
     for (int t = lane; t < n; t += 32) acc[t] = 0.0;
     __syncwarp();
     bool bad = false;
-    // 1) presence bitmap of the row's columns
+    // 1) presence bitmap of the row's columns (native 32-bit shared atomicOr)
     walk_row_k_sequential<false>(A, B, rs, re, [&](int j, double, double) {
       if (upper && j < ig) return;
       const unsigned off = (unsigned)(j - lo);
@@ -162,38 +166,33 @@ __global__ void __launch_bounds__(WPB * 32) num_warp_rank_kernel(
         bad = true;
         return;
       }
-      atomicOr(&bm[off >> 5], 1u << (off & 31));
+      atomicOr(&bm32[off >> 5], 1u << (off & 31));
     });
-    // 2) exclusive popcount prefix per word
+    // 2) exclusive popcount prefix per 64-bit word
     int running = 0;
     for (int w0 = 0; w0 < W; w0 += 32) {
       const int w = w0 + lane;
-      const int c = (w < W) ? __popc(bm[w]) : 0;
+      const int c = (w < W) ? __popcll(bm[w]) : 0;
       const int incl = warp_incl_scan(c);
       if (w < W) pre[w] = (unsigned short)(running + incl - c);
       running += __shfl_sync(kFull, incl, 31);
     }
     __syncwarp();
     if (running != n) bad = true;
-    // 3) accumulate at the column's rank, k by k
+    // 3) accumulate at the column's rank, k by k; remember the column of every rank
     if (running == n) {
       walk_row_k_sequential<true>(A, B, rs, re, [&](int j, double x, double a) {
         if (upper && j < ig) return;
         const unsigned off = (unsigned)(j - lo);
         if (off >= (unsigned)span) return;
-        const unsigned w = off >> 5;
-        const int pos = pre[w] + __popc(bm[w] & ((1u << (off & 31)) - 1u));
+        const unsigned w = off >> 6;
+        const int pos = pre[w] + __popcll(bm[w] & ((1ull << (off & 63)) - 1ull));
         acc[pos] = mul_add_rn(acc[pos], a, x);
+        col[pos] = j;
       });
-      // 4) ordered output: t-th set bit of the bitmap and its sum
+      // 4) the row is already in column order: one coalesced copy
       for (int t = lane; t < n; t += 32) {
-        int lo_w = 0, hi_w = W - 1;
-        while (lo_w < hi_w) {
-          const int mid = (lo_w + hi_w + 1) >> 1;
-          if ((int)pre[mid] <= t) lo_w = mid; else hi_w = mid - 1;
-        }
-        const int off = lo_w * 32 + nth_set_bit(bm[lo_w], t - pre[lo_w]);
-        cci[c0 + t] = lo + off;
+        cci[c0 + t] = col[t];
         cval[c0 + t] = acc[t];
       }
     }
@@ -478,15 +477,15 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
                              err, num_sms, s);
       break;
     case kNumRank2K:
-      run_warp_rank<2048, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
+      run_warp_rank<2304, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
                              cval, err, num_sms, s);
       break;
     case kNumRank4K:
-      run_warp_rank<4096, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
+      run_warp_rank<4608, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
                              cval, err, num_sms, s);
       break;
     case kNumRank8K:
-      run_warp_rank<8192, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
+      run_warp_rank<9216, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
                              cval, err, num_sms, s);
       break;
     case kNumHashBlock: {

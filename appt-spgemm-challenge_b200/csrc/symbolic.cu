@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(WPB * 32) sym_warp_kernel(const int* rows, con
 // Warp per row, bitmap over [lo, hi] (at most WORDS words), filled k-sequentially with
 // fire-and-forget atomicOr (no return value needed), then counted with one popcount pass.
 template <int WORDS, int WPB>
-__global__ void __launch_bounds__(WPB * 32) sym_warp_bitmap_kernel(
+__global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? 6 : 3) sym_warp_bitmap_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
     const int* lo_arr, const int* hi_arr, int* row_nnz, int* err) {
   extern __shared__ unsigned sym_smem[];

@@ -27,34 +27,47 @@ __device__ __forceinline__ void walk_row_k_sequential(const Csr& A, const Csr& B
     const int len = v ? B.rp[k + 1] - bs : 0;
     const double a = (WITH_VAL && v) ? A.val[p] : 0.0;
     const int cnt = (re - base) < 32 ? (re - base) : 32;
-    int bs_c = __shfl_sync(kFull, bs, 0);
-    int len_c = __shfl_sync(kFull, len, 0);
-    double a_c = WITH_VAL ? __shfl_sync(kFull, a, 0) : 0.0;
-    int j_c = (lane < len_c) ? B.ci[bs_c + lane] : 0;
-    double x_c = (WITH_VAL && lane < len_c) ? B.val[bs_c + lane] : 0.0;
-    for (int t = 0; t < cnt; ++t) {
-      const int tn = (t + 1) & 31;
-      const int bs_n = __shfl_sync(kFull, bs, tn);
-      const int len_n = (t + 1 < cnt) ? __shfl_sync(kFull, len, tn) : 0;
-      const double a_n = WITH_VAL ? __shfl_sync(kFull, a, tn) : 0.0;
-      int j_n = 0;
-      double x_n = 0.0;
-      if (lane < len_n) {
-        j_n = B.ci[bs_n + lane];
-        if (WITH_VAL) x_n = B.val[bs_n + lane];
+    // pipeline: the (j, b_kj) pairs of the next two rows of B are loaded ahead; j = -1 marks
+    // a lane without an entry
+    int j0 = -1, j1 = -1;
+    double x0 = 0.0, x1 = 0.0;
+    {
+      const int b0 = __shfl_sync(kFull, bs, 0), l0 = __shfl_sync(kFull, len, 0);
+      const int b1 = __shfl_sync(kFull, bs, 1);
+      const int l1 = cnt > 1 ? __shfl_sync(kFull, len, 1) : 0;
+      if (lane < l0) {
+        j0 = B.ci[b0 + lane];
+        if (WITH_VAL) x0 = B.val[b0 + lane];
       }
-      if (lane < len_c) f(j_c, x_c, a_c);
-      for (int q = 32 + lane; q < len_c; q += 32) {   // rows of B longer than a warp
-        const int j = B.ci[bs_c + q];
-        const double x = WITH_VAL ? B.val[bs_c + q] : 0.0;
-        f(j, x, a_c);
+      if (lane < l1) {
+        j1 = B.ci[b1 + lane];
+        if (WITH_VAL) x1 = B.val[b1 + lane];
+      }
+    }
+    for (int t = 0; t < cnt; ++t) {
+      const int t2 = (t + 2) & 31;
+      const int b2 = __shfl_sync(kFull, bs, t2);
+      const int l2 = (t + 2 < cnt) ? __shfl_sync(kFull, len, t2) : 0;
+      int j2 = -1;
+      double x2 = 0.0;
+      if (lane < l2) {
+        j2 = B.ci[b2 + lane];
+        if (WITH_VAL) x2 = B.val[b2 + lane];
+      }
+      const double at = WITH_VAL ? __shfl_sync(kFull, a, t) : 0.0;
+      if (j0 >= 0) f(j0, x0, at);
+      const int lt = __shfl_sync(kFull, len, t);
+      if (lt > 32) {                      // rows of B longer than a warp (warp-uniform branch)
+        const int bt = __shfl_sync(kFull, bs, t);
+        for (int q = 32 + lane; q < lt; q += 32) {
+          const int j = B.ci[bt + q];
+          const double x = WITH_VAL ? B.val[bt + q] : 0.0;
+          f(j, x, at);
+        }
       }
       __syncwarp();
-      bs_c = bs_n;
-      len_c = len_n;
-      a_c = a_n;
-      j_c = j_n;
-      x_c = x_n;
+      j0 = j1; x0 = x1;
+      j1 = j2; x1 = x2;
     }
   }
 }

@@ -96,12 +96,12 @@ def test_all_tiers(tier_matrix, method):
 
 
 @pytest.mark.parametrize("method", ["adaptive", "hash", "esc"])
-@pytest.mark.parametrize("name", ["uniform8", "stencil27", "banded", "rmat"])
+@pytest.mark.parametrize("name", ["uniform8", "stencil27", "banded", "random"])
 def test_sequential_tiers_are_bit_exact(name, method):
     """The warp tiers (rank, warp hash) and ESC sum each column in the reference's k-then-j
     order with separate multiply and add roundings, so their values equal the oracle's bit for
     bit (the CTA tiers, used only for rows beyond 512 entries, accumulate with atomics)."""
-    A = M.make(name, small=True)
+    A = M.random_csr(2000, 2000, 0.005, 4) if name == "random" else M.make(name, small=True)
     C, st = ap.spgemm(A, method=method, return_stats=True)
     assert st["bin_rows"]["hash_block"] == 0 and st["bin_rows"]["window"] == 0
     R = oracle.spgemm(A)
