@@ -192,6 +192,21 @@ int appt_estimate_row_nnz(const appt_csr *A, int32_t att, const appt_options *op
  * reference picks its hash path when the score is negative. */
 double appt_reference_score(const int32_t *row_ptr, int64_t rows, int64_t nnz);
 
+/* C = A * B (B = A when NULL) for device-resident A and B, written into device buffers the
+ * caller owns, without allocating any memory: for callers that cannot call cudaMalloc during the
+ * multiply (a framework whose allocator owns the device heap, code where allocation is
+ * forbidden, loops that pre-size every buffer). No counterpart in the reference.
+ * C_row_ptr: A->rows + 1 int64; C_col_idx / C_val: room for C_capacity entries. Fills
+ * C_row_ptr and *C_nnz_out; returns APPT_ERR_TOO_LARGE before the numeric phase when nnz(C) >
+ * C_capacity (size the buffers and call again). Temporaries live in one fixed 64 MiB device
+ * array owned by the library (present on every GPU that loads it, until exit), which limits A
+ * to about 2.2 million rows (larger A: APPT_ERR_TOO_LARGE with a message). The first call on a
+ * device resolves that array's address and should come before any stream capture. Calls share
+ * the array; this function serialises them per device and waits for its own GPU work. */
+int appt_spgemm_noalloc(const appt_csr *A, const appt_csr *B, int64_t *C_row_ptr,
+                        int32_t *C_col_idx, double *C_val, int64_t C_capacity,
+                        int64_t *C_nnz_out, void *stream);
+
 const char *appt_last_error(void);
 int appt_device_count(void);
 int64_t appt_kernel_launches(void); /* kernels launched by this process so far */
