@@ -157,39 +157,17 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? 6 : 7)
     for (int w = lane; w < W; w += 32) bm[w] = 0ull;
     for (int t = lane; t < n; t += 32) acc[t] = 0.0;
     __syncwarp();
-    bool bad = false;
+    const int jmin = upper ? ig : 0;
     // 1) presence bitmap of the row's columns (native 32-bit shared atomicOr)
-    walk_row_k_sequential<false>(A, B, rs, re, [&](int j, double, double) {
-      if (upper && j < ig) return;
-      const unsigned off = (unsigned)(j - lo);
-      if (off >= (unsigned)span) {
-        bad = true;
-        return;
-      }
-      atomicOr(&bm32[off >> 5], 1u << (off & 31));
-    });
+    bool bad = fill_row_bitmap(A, B, rs, re, lo, (unsigned)span, jmin, bm32);
+    __syncwarp();
     // 2) exclusive popcount prefix per 64-bit word
-    int running = 0;
-    for (int w0 = 0; w0 < W; w0 += 32) {
-      const int w = w0 + lane;
-      const int c = (w < W) ? __popcll(bm[w]) : 0;
-      const int incl = warp_incl_scan(c);
-      if (w < W) pre[w] = (unsigned short)(running + incl - c);
-      running += __shfl_sync(kFull, incl, 31);
-    }
+    const int running = bitmap_prefix64(bm, W, pre);
     __syncwarp();
     if (running != n) bad = true;
     // 3) accumulate at the column's rank, k by k; remember the column of every rank
     if (running == n) {
-      walk_row_k_sequential<true>(A, B, rs, re, [&](int j, double x, double a) {
-        if (upper && j < ig) return;
-        const unsigned off = (unsigned)(j - lo);
-        if (off >= (unsigned)span) return;
-        const unsigned w = off >> 6;
-        const int pos = pre[w] + __popcll(bm[w] & ((1ull << (off & 63)) - 1ull));
-        acc[pos] = mul_add_rn(acc[pos], a, x);
-        col[pos] = j;
-      });
+      accumulate_row_ranked(A, B, rs, re, lo, (unsigned)span, jmin, bm, pre, acc, col);
       // 4) the row is already in column order: one coalesced copy
       for (int t = lane; t < n; t += 32) {
         cci[c0 + t] = col[t];

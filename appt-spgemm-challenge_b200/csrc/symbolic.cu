@@ -152,16 +152,9 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? 6 : 3) sym_warp_bitm
     }
     for (int w = lane; w < W; w += 32) bm[w] = 0u;
     __syncwarp();
-    bool bad = false;
-    walk_row_k_sequential<false>(A, B, A.rp[i], A.rp[i + 1], [&](int j, double, double) {
-      if (upper && j < ig) return;
-      const unsigned off = (unsigned)(j - lo);
-      if (off >= (unsigned)span) {
-        bad = true;
-        return;
-      }
-      atomicOr(&bm[off >> 5], 1u << (off & 31));
-    });
+    const bool bad = fill_row_bitmap(A, B, A.rp[i], A.rp[i + 1], lo, (unsigned)span,
+                                     upper ? ig : 0, bm);
+    __syncwarp();
     int cnt = 0;
     for (int w = lane; w < W; w += 32) cnt += __popc(bm[w]);
     cnt = warp_sum(cnt);
