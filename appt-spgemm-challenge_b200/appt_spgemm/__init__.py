@@ -29,9 +29,12 @@ LIB_PATH = PKG_DIR / "libappt_spgemm.so"
 OPS = {"ab": 0, "aat": 1, "aat_upper": 2, "ab_upper": 3}
 METHODS = {"adaptive": 0, "hash": 1, "merge": 2, "esc": 3}
 MEM_HOST, MEM_DEVICE = 0, 1
-NUM_BINS = 16
-BIN_NAMES = ["rank2k", "rank4k", "rank8k", "hash64", "hash128", "hash256", "hash512", "hash1024",
-             "hash_block", "window", "merge"]
+NUM_BINS = 32
+# Numeric tiers in bin order; the rank tiers come in three walks each (1, 2 or 4 lane groups
+# per warp, chosen by the average length of the row's B rows).
+BIN_NAMES = ["rank2k_g1", "rank2k_g2", "rank2k_g4", "rank4k_g1", "rank4k_g2", "rank4k_g4",
+             "rank8k_g1", "rank8k_g2", "rank8k_g4", "hash64", "hash128", "hash256", "hash512",
+             "hash1024", "hash_block", "window", "merge"]
 PHASES = ["h2d", "transpose", "analyze", "symbolic", "scan", "numeric", "d2h", "other"]
 
 # Reference entry points exported with C linkage (include/appt_spgemm.h, layer 1).
@@ -58,6 +61,15 @@ class CsrOut(ct.Structure):
                 ("mem", ct.c_int32), ("device", ct.c_int32), ("opaque", ct.c_void_p)]
 
 
+def _tier_rows(bin_rows) -> dict:
+    """Rows per tier, the lane-group variants of a tier summed (rank2k_g1 + _g2 + _g4 -> rank2k)."""
+    out: dict = {}
+    for i, name in enumerate(BIN_NAMES):
+        tier = name.split("_g")[0]
+        out[tier] = out.get(tier, 0) + int(bin_rows[i])
+    return out
+
+
 class Stats(ct.Structure):
     _fields_ = [("products", ct.c_int64), ("c_nnz", ct.c_int64),
                 ("bin_rows", ct.c_int64 * NUM_BINS), ("ms_total", ct.c_double),
@@ -69,6 +81,7 @@ class Stats(ct.Structure):
             "products": int(self.products),
             "c_nnz": int(self.c_nnz),
             "bin_rows": {BIN_NAMES[i]: int(self.bin_rows[i]) for i in range(len(BIN_NAMES))},
+            "tier_rows": _tier_rows(self.bin_rows),
             "ms_total": float(self.ms_total),
             "ms_phase": {PHASES[i]: float(self.ms_phase[i]) for i in range(8)},
             "kernel_launches": int(self.kernel_launches),
@@ -108,6 +121,9 @@ def load() -> ct.CDLL:
     lib.appt_free_out.restype = ct.c_int
     lib.appt_transpose.argtypes = [ct.POINTER(CsrIn), ct.POINTER(Options), ct.POINTER(CsrOut)]
     lib.appt_transpose.restype = ct.c_int
+    lib.appt_transpose_into.argtypes = [ct.POINTER(CsrIn), ct.POINTER(Options), ct.c_void_p,
+                                        ct.c_void_p, ct.c_void_p]
+    lib.appt_transpose_into.restype = ct.c_int
     lib.appt_row_products.argtypes = [ct.POINTER(CsrIn), ct.POINTER(CsrIn), ct.POINTER(Options),
                                       ct.c_void_p]
     lib.appt_row_products.restype = ct.c_int
@@ -270,6 +286,19 @@ def transpose(A: Csr, device: int = 0) -> Csr:
         return _take_host_out(out)
     finally:
         lib.appt_free_out(ct.byref(out))
+
+
+def transpose_into_device(rows: int, cols: int, nnz: int, row_ptr: int, col_idx: int, val: int,
+                          t_row_ptr: int, t_col_idx: int, t_val: int, stream: int | None = None,
+                          device: int = 0) -> None:
+    """A^T of a device-resident A into caller-allocated device buffers (int32 row_ptr of
+    cols + 1 entries, nnz column indices and values) -- the operand format, so it can be passed
+    as B of spgemm_device."""
+    lib = load()
+    a = CsrIn(rows, cols, nnz, row_ptr, col_idx, val)
+    o = _options("ab", "adaptive", MEM_DEVICE, MEM_DEVICE, 0, stream, device)
+    _check(lib.appt_transpose_into(ct.byref(a), ct.byref(o), t_row_ptr, t_col_idx, t_val),
+           "appt_transpose_into")
 
 
 def row_products(A: Csr, B: Csr | None = None, device: int = 0) -> np.ndarray:

@@ -24,6 +24,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=default",
           f"-I{INCLUDE}", f"-I{CSRC}"]
+# Tuning constants (e.g. APPT_NVCC_DEFINES="APPT_RANK_MIN_BLOCKS=5") become -D flags.
+COMMON += [f"-D{d}" for d in os.environ.get("APPT_NVCC_DEFINES", "").split() if d]
 
 
 def _sources():
@@ -51,6 +53,11 @@ def _compile(src: Path, verbose: bool, ptxas_info: bool) -> tuple[Path, str]:
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
     BUILD.mkdir(exist_ok=True)
     hdr = _headers_mtime()
+    stamp = BUILD / "flags.txt"
+    flags = " ".join(ARCH + COMMON)
+    if not stamp.exists() or stamp.read_text() != flags:
+        force = True
+        stamp.write_text(flags)
     srcs = _sources()
     todo = []
     for s in srcs:

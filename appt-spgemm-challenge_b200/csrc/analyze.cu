@@ -17,13 +17,13 @@ namespace {
 
 constexpr int kAnThreads = 256;
 
-__device__ __forceinline__ int sym_bin_of(long long flop, long long span) {
+__device__ __forceinline__ int sym_bin_of(long long flop, long long span, long long rowlen) {
   if (flop == 0 || span <= 0) return 255;
   const long long W = (span + 31) >> 5;
   if (W <= 4096 && W <= 8 * flop + 64) {       // bitmap: clearing/counting W words pays off
-    if (W <= 256) return kSymBmS;
-    if (W <= 1024) return kSymBmM;
-    return kSymBmL;
+    if (W <= 256) return kSymBmS + group_index(flop, rowlen);
+    if (W <= 1024) return kSymBmM + group_index(flop, rowlen);
+    return kSymBmL + group_index(flop, rowlen);
   }
   if (flop <= (1ll << 26)) {
     if (2 * flop <= 256) return kSymHashS;
@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(kAnThreads) analyze_kernel(Csr A, Csr B, int u
       } else if (method == kMethodMerge && rowlen <= kMergeMaxLists) {
         key = (f > 0 && span > 0) ? kNumSymBins : 255;   // the merge-count bin
       } else {
-        key = sym_bin_of(f, span);
+        key = sym_bin_of(f, span, rowlen);
       }
       symkey[row] = (uint8_t)key;
       if (key == 255) row_nnz[row] = 0;
@@ -133,11 +133,11 @@ __device__ __forceinline__ int num_bin_of(int method, long long nnz, long long f
   if (nnz == 0) return 255;
   if (method == kMethodMerge && rowlen <= kMergeMaxLists) return kNumMerge;
   if (method == kMethodAdaptive) {
-    const long long W = (span + 63) >> 6;
-    const long long bytes = ((10 * W + 7) & ~7ll) + 12 * nnz;  // bitmap, prefix, sums, columns
-    if (bytes <= 2304) return kNumRank2K;
-    if (bytes <= 4608) return kNumRank4K;
-    if (bytes <= 9216) return kNumRank8K;
+    const long long W = (span + 31) >> 5;
+    const long long bytes = ((6 * W + 7) & ~7ll) + 10 * nnz;   // bitmap, prefix, sums, columns
+    if (bytes <= 2304) return kNumRank2K + group_index(flop, rowlen);
+    if (bytes <= 4608) return kNumRank4K + group_index(flop, rowlen);
+    if (bytes <= 9216) return kNumRank8K + group_index(flop, rowlen);
     if (nnz > 512 && span <= kWindowCols && span <= 4 * nnz) return kNumWindow;
   }
   if (nnz <= 32) return kNumHash64;

@@ -219,6 +219,14 @@ int appt_transpose(const appt_csr* A, const appt_options* opt, appt_csr_out* AT)
   return APPT_OK;
 }
 
+int appt_transpose_into(const appt_csr* A, const appt_options* opt, int32_t* t_row_ptr,
+                        int32_t* t_col_idx, double* t_val) {
+  if (!A) return APPT_ERR_INVALID;
+  appt_options def;
+  appt_default_options(&def);
+  return appt::transpose_into(view_of(A), opts_of(opt ? opt : &def), t_row_ptr, t_col_idx, t_val);
+}
+
 int appt_row_products(const appt_csr* A, const appt_csr* B, const appt_options* opt,
                       int64_t* out) {
   if (!A || !out) return APPT_ERR_INVALID;

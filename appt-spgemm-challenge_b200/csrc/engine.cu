@@ -111,6 +111,7 @@ struct Scratch {
   DeviceCtx* ctx;
   cudaStream_t s;
   std::vector<void*> ptrs;
+  std::vector<std::vector<int>> host_keep;   // host staging copies alive until the call ends
   bool failed = false;
   Scratch(DeviceCtx* c, cudaStream_t st) : ctx(c), s(st) {}
   template <typename T>
@@ -389,7 +390,7 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   }
   if (st) {
     st->products = (long long)hst.total_flop;
-    for (int b = 0; b < kNumNumBins && b < 16; ++b) st->bin_rows[b] = boff[b + 1] - boff[b];
+    for (int b = 0; b < kNumNumBins && b < 32; ++b) st->bin_rows[b] = boff[b + 1] - boff[b];
   }
   int* cci = sc.get<int>(nnz);
   double* cval = sc.get<double>(nnz);
@@ -406,7 +407,7 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
       launch_merge_numeric(rows_num, boff_num, b, nr, A, B, upper, row_base, crp, cci, cval, err,
                            sms, s);
     else
-      launch_numeric(b, rows_num, boff_num, nr, A, B, upper, row_base, lo, hi, crp, cci, cval,
+      launch_numeric(b, rows_num, boff_num, nr, A, B, upper, row_base, lo, hi, flop, crp, cci, cval,
                      err, sms, s);
     note_launches(1);
   }
@@ -443,10 +444,21 @@ static int stage_operand(const MatView& M, Scratch& sc, cudaStream_t s, Csr* out
     set_error("device pool allocation failed for an operand");
     return kErrOom;
   }
-  CK(cudaMemcpyAsync(rp, M.rp, sizeof(int) * ((size_t)M.rows + 1), cudaMemcpyHostToDevice, s));
+  // A host row block (row_ptr[0] != 0) is staged from col_idx + row_ptr[0] with its row pointers
+  // rebased to 0, so the device copy holds exactly the block's entries.
+  const int rp0 = M.rp[0];
+  if (rp0 == 0) {
+    CK(cudaMemcpyAsync(rp, M.rp, sizeof(int) * ((size_t)M.rows + 1), cudaMemcpyHostToDevice, s));
+  } else {
+    sc.host_keep.emplace_back((size_t)M.rows + 1);
+    std::vector<int>& rb = sc.host_keep.back();
+    for (long long i = 0; i <= M.rows; ++i) rb[(size_t)i] = M.rp[i] - rp0;
+    CK(cudaMemcpyAsync(rp, rb.data(), sizeof(int) * rb.size(), cudaMemcpyHostToDevice, s));
+  }
   if (M.nnz > 0) {
-    CK(cudaMemcpyAsync(ci, M.ci, sizeof(int) * (size_t)M.nnz, cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(val, M.val, sizeof(double) * (size_t)M.nnz, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(ci, M.ci + rp0, sizeof(int) * (size_t)M.nnz, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(val, M.val + rp0, sizeof(double) * (size_t)M.nnz, cudaMemcpyHostToDevice,
+                       s));
   }
   out->rp = rp;
   out->ci = ci;
@@ -766,6 +778,41 @@ int transpose(const MatView& A, const CallOptions& opt, MatOut* AT) {
   AT->mem = 0;
   AT->alloc_kind = 3;
   AT->base = h;
+  return kOk;
+}
+
+int transpose_into(const MatView& A, const CallOptions& opt, int* t_rp, int* t_ci,
+                   double* t_val) {
+  if (!t_rp || (A.nnz > 0 && (!t_ci || !t_val))) {
+    set_error("appt_transpose_into: null output buffer");
+    return kErrInvalid;
+  }
+  int rc = check_view(A, opt.in_mem, "A");
+  if (rc) return rc;
+  DeviceCtx* ctx = nullptr;
+  rc = get_ctx(opt.device, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  CK(cudaSetDevice(opt.device));
+  cudaStream_t s = opt.stream ? (cudaStream_t)opt.stream : ctx->stream;
+  Scratch sc(ctx, s);
+  Csr dA{};
+  if (opt.in_mem == 0) {
+    rc = stage_operand(A, sc, s, &dA);
+    if (rc) return rc;
+  } else {
+    dA = Csr{A.rp, A.ci, A.val, (int)A.rows, (int)A.cols};
+  }
+  Csr T{};
+  rc = do_transpose(ctx, dA, A.nnz, sc, s, &T, false);
+  if (rc) return rc;
+  const cudaMemcpyKind kind = opt.in_mem == 0 ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+  CK(cudaMemcpyAsync(t_rp, T.rp, sizeof(int) * ((size_t)A.cols + 1), kind, s));
+  if (A.nnz > 0) {
+    CK(cudaMemcpyAsync(t_ci, T.ci, sizeof(int) * (size_t)A.nnz, kind, s));
+    CK(cudaMemcpyAsync(t_val, T.val, sizeof(double) * (size_t)A.nnz, kind, s));
+  }
+  CK(cudaStreamSynchronize(s));
   return kOk;
 }
 

@@ -41,7 +41,7 @@ struct MatOut {           // CSR result with int64 row pointers
 struct CallStats {
   long long products = 0;
   long long c_nnz = 0;
-  long long bin_rows[16] = {0};
+  long long bin_rows[32] = {0};
   double ms_total = 0.0;
   double ms_phase[8] = {0};   // h2d, transpose, analyze, symbolic, scan, numeric, d2h, other
   long long launches = 0;
@@ -64,6 +64,7 @@ int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C
            CallStats* stats);
 int free_out(MatOut* C);
 int transpose(const MatView& A, const CallOptions& opt, MatOut* AT);
+int transpose_into(const MatView& A, const CallOptions& opt, int* t_rp, int* t_ci, double* t_val);
 int row_products(const MatView& A, const MatView* B, const CallOptions& opt, long long* out);
 int estimate_row_nnz(const MatView& A, int att, const CallOptions& opt, int* out);
 double reference_score(const int* row_ptr, long long rows, long long nnz);

@@ -7,7 +7,7 @@
 
 namespace appt {
 
-constexpr int kMaxBins = 16;
+constexpr int kMaxBins = 32;
 
 // Capacities shared by the classifier and the kernels.
 constexpr int kWindowCols = 16384;      // CTA window tier: columns per window
@@ -15,12 +15,20 @@ constexpr int kHashBlockSlots = 8192;   // CTA hash tier: table slots (rows with
 constexpr int kSymBlockWords = 32768;   // CTA symbolic bitmap window: 2^20 columns
 constexpr int kMergeMaxLists = 256;     // merge tier: rows with more A entries use other tiers
 
+// Lane groups of the warp walks (walk.cuh): a row whose B rows average <= 8 entries is walked by
+// 4 groups of 8 lanes, <= 16 by 2 groups of 16, longer by the whole warp. Tiers that walk
+// k-sequentially come in one bin per group count (index 0, 1, 2 for G = 1, 2, 4).
+__host__ __device__ __forceinline__ int group_index(long long flop, long long rowlen) {
+  const long long avg = rowlen > 0 ? flop / rowlen : 32;
+  return avg <= 8 ? 2 : avg <= 16 ? 1 : 0;
+}
+
 // ---- symbolic bins (chosen per row from products count and column span) ----
 enum SymBin : int {
-  kSymBmS = 0,     // warp per row, bitmap over the span, <= 256 words   (k-sequential)
-  kSymBmM,         //                                      <= 1024 words
-  kSymBmL,         //                                      <= 4096 words
-  kSymHashS,       // warp per row, key hash of 256 / 1024 / 4096 slots (wide spans)
+  kSymBmS = 0,     // warp per row, bitmap over the span, <= 256 words   (k-sequential), x3 G
+  kSymBmM = 3,     //                                      <= 1024 words
+  kSymBmL = 6,     //                                      <= 4096 words
+  kSymHashS = 9,   // warp per row, key hash of 256 / 1024 / 4096 slots (wide spans)
   kSymHashM,
   kSymHashL,
   kSymBlock,       // CTA per row, 2^20-column bitmap windows (any row)
@@ -29,10 +37,10 @@ enum SymBin : int {
 
 // ---- numeric bins (chosen per row from exact nnz, products count and span) ----
 enum NumBin : int {
-  kNumRank2K = 0,  // warp per row, bitmap-rank accumulator in 2 / 4 / 8 KB of shared memory
-  kNumRank4K,
-  kNumRank8K,
-  kNumHash64,      // warp per row, hash tables of 64 .. 1024 slots + in-smem sort
+  kNumRank2K = 0,  // warp per row, bitmap-rank accumulator in 2 / 4 / 8 KB of shared memory,
+  kNumRank4K = 3,  // each x3 lane-group counts
+  kNumRank8K = 6,
+  kNumHash64 = 9,  // warp per row, hash tables of 64 .. 1024 slots + in-smem sort
   kNumHash128,
   kNumHash256,
   kNumHash512,
@@ -85,7 +93,7 @@ void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, 
 // numeric.cu
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows_host,
                     Csr A, Csr B, int upper, int row_base, const int* lo, const int* hi,
-                    const long long* crp, int* cci, double* cval, int* err, int num_sms,
+                    const long long* flop, const long long* crp, int* cci, double* cval, int* err, int num_sms,
                     cudaStream_t s);
 
 // merge.cu

@@ -205,7 +205,8 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
   for (int b = 0; b < kNumNumBins; ++b) {
     const long long nr = boff[b + 1] - boff[b];
     if (nr <= 0) continue;
-    launch_numeric(b, rows_num, boff_num, nr, dA, dB, 0, 0, lo, hi, crp, cci, cval, err, sms, s);
+    launch_numeric(b, rows_num, boff_num, nr, dA, dB, 0, 0, lo, hi, flop, crp, cci, cval, err, sms,
+                   s);
     note_launches(1);
   }
   e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s);

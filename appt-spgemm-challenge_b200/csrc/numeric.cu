@@ -117,18 +117,23 @@ __global__ void __launch_bounds__(WPB * 32, 2048 / (WPB * 32) * 3 / 4) num_warp_
 }
 
 // --------------------------------------------------------------------------- warp rank tier
-// Row layout in the warp's shared budget: bitmap over [lo, hi] in 64-bit words (W words), a
+// Row layout in the warp's shared budget: bitmap over [lo, hi] in 32-bit words (W words), a
 // 16-bit exclusive popcount prefix per word, the fp64 accumulator of the row's nnz entries and
-// the column of every rank (so the finished row is copied out coalesced).
+// the 16-bit column offset (j - lo) of every rank, so the finished row is copied out coalesced.
 // The bitmap is rebuilt from the products, after which the output position of column j is
 // prefix[w] + popcount(bitmap[w] & below(j)) -- values accumulate directly in output order, so
-// the row needs neither a hash table nor a sort. Products are visited k-sequentially
-// (walk.cuh): no atomics on the accumulator, and every sum forms in the reference's order.
-template <int BUDGET, int WPB>
-__global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? 6 : 7)
+// the row needs neither a hash table nor a sort. Products are visited k-sequentially (walk.cuh),
+// by G lane groups when the row's B rows are short: no atomics on the accumulator, and every sum
+// forms in the reference's order.
+#ifndef APPT_RANK_MIN_BLOCKS
+#define APPT_RANK_MIN_BLOCKS 5  // resident 256-thread CTAs per SM the register budget targets
+#endif
+template <int BUDGET, int WPB, int G>
+__global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCKS : 7)
     num_warp_rank_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
-    const int* lo_arr, const int* hi_arr, const long long* crp, int* cci, double* cval, int* err) {
+    const int* lo_arr, const int* hi_arr, const long long* crp, int* cci, double* cval,
+    int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned char* base = num_smem + (size_t)warp * BUDGET;
@@ -143,34 +148,33 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? 6 : 7)
     const int rs = A.rp[i], re = A.rp[i + 1];
     const long long c0 = crp[i];
     const int n = (int)(crp[i + 1] - c0);
-    const int W = (int)((span + 63) >> 6);
-    const int acc_off = ((10 * W) + 7) & ~7;
-    if (span <= 0 || acc_off + 12 * n > BUDGET || n > 65535) {
+    const int W = (int)((span + 31) >> 5);
+    const int acc_off = ((6 * W) + 7) & ~7;
+    if (span <= 0 || span > 65536 || acc_off + 10 * n > BUDGET) {
       if (lane == 0) set_error(err, kErrCapacity);
       continue;
     }
-    unsigned long long* bm = reinterpret_cast<unsigned long long*>(base);
-    unsigned* bm32 = reinterpret_cast<unsigned*>(base);              // same bits, 32-bit view
-    unsigned short* pre = reinterpret_cast<unsigned short*>(base + 8 * W);
+    unsigned* bm = reinterpret_cast<unsigned*>(base);
+    unsigned short* pre = reinterpret_cast<unsigned short*>(base + 4 * W);
     double* acc = reinterpret_cast<double*>(base + acc_off);
-    int* col = reinterpret_cast<int*>(base + acc_off + 8 * n);
-    for (int w = lane; w < W; w += 32) bm[w] = 0ull;
+    unsigned short* coff = reinterpret_cast<unsigned short*>(base + acc_off + 8 * n);
+    for (int w = lane; w < W; w += 32) bm[w] = 0u;
     for (int t = lane; t < n; t += 32) acc[t] = 0.0;
     __syncwarp();
     const int jmin = upper ? ig : 0;
     // 1) presence bitmap of the row's columns (native 32-bit shared atomicOr)
-    bool bad = fill_row_bitmap(A, B, rs, re, lo, (unsigned)span, jmin, bm32);
+    bool bad = fill_row_bitmap_g<G>(A, B, rs, re, lo, (unsigned)span, jmin, bm);
     __syncwarp();
-    // 2) exclusive popcount prefix per 64-bit word
-    const int running = bitmap_prefix64(bm, W, pre);
+    // 2) exclusive popcount prefix per word
+    const int running = bitmap_prefix32(bm, W, pre);
     __syncwarp();
     if (running != n) bad = true;
     // 3) accumulate at the column's rank, k by k; remember the column of every rank
     if (running == n) {
-      accumulate_row_ranked(A, B, rs, re, lo, (unsigned)span, jmin, bm, pre, acc, col);
+      accumulate_row_ranked_g<G>(A, B, rs, re, lo, (unsigned)span, jmin, bm, pre, acc, coff);
       // 4) the row is already in column order: one coalesced copy
       for (int t = lane; t < n; t += 32) {
-        cci[c0 + t] = col[t];
+        cci[c0 + t] = lo + (int)coff[t];
         cval[c0 + t] = acc[t];
       }
     }
@@ -409,13 +413,13 @@ void run_warp_hash(int bin, const int* rows, const long long* bin_off, long long
                                     err);
 }
 
-template <int BUDGET, int WPB>
-void run_warp_rank(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
-                   Csr B, int upper, int row_base, const int* lo, const int* hi,
-                   const long long* crp, int* cci, double* cval, int* err, int num_sms,
-                   cudaStream_t s) {
+template <int BUDGET, int WPB, int G>
+void run_warp_rank_g(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
+                     Csr B, int upper, int row_base, const int* lo, const int* hi,
+                     const long long* crp, int* cci, double* cval, int* err, int num_sms,
+                     cudaStream_t s) {
   const size_t smem = (size_t)WPB * BUDGET;
-  auto kern = num_warp_rank_kernel<BUDGET, WPB>;
+  auto kern = num_warp_rank_kernel<BUDGET, WPB, G>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -426,13 +430,46 @@ void run_warp_rank(int bin, const int* rows, const long long* bin_off, long long
                                     cval, err);
 }
 
+// bin = tier base + group index (0, 1, 2 for G = 1, 2, 4)
+template <int BUDGET, int WPB>
+void run_warp_rank(int bin, int gidx, const int* rows, const long long* bin_off, long long nrows,
+                   Csr A, Csr B, int upper, int row_base, const int* lo, const int* hi,
+                   const long long* crp, int* cci, double* cval, int* err, int num_sms,
+                   cudaStream_t s) {
+  if (gidx == 2)
+    run_warp_rank_g<BUDGET, WPB, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp,
+                                    cci, cval, err, num_sms, s);
+  else if (gidx == 1)
+    run_warp_rank_g<BUDGET, WPB, 2>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp,
+                                    cci, cval, err, num_sms, s);
+  else
+    run_warp_rank_g<BUDGET, WPB, 1>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp,
+                                    cci, cval, err, num_sms, s);
+}
+
 }  // namespace
 
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
                     Csr B, int upper, int row_base, const int* lo, const int* hi,
-                    const long long* crp, int* cci, double* cval, int* err, int num_sms,
+                    const long long* flop, const long long* crp, int* cci, double* cval, int* err, int num_sms,
                     cudaStream_t s) {
   if (nrows <= 0) return;
+  (void)flop;
+  if (bin >= kNumRank2K && bin < kNumRank2K + 3) {
+    run_warp_rank<2304, 8>(bin, bin - kNumRank2K, rows, bin_off, nrows, A, B, upper, row_base, lo,
+                           hi, crp, cci, cval, err, num_sms, s);
+    return;
+  }
+  if (bin >= kNumRank4K && bin < kNumRank4K + 3) {
+    run_warp_rank<4608, 8>(bin, bin - kNumRank4K, rows, bin_off, nrows, A, B, upper, row_base, lo,
+                           hi, crp, cci, cval, err, num_sms, s);
+    return;
+  }
+  if (bin >= kNumRank8K && bin < kNumRank8K + 3) {
+    run_warp_rank<9216, 4>(bin, bin - kNumRank8K, rows, bin_off, nrows, A, B, upper, row_base, lo,
+                           hi, crp, cci, cval, err, num_sms, s);
+    return;
+  }
   switch (bin) {
     case kNumHash64:
       run_warp_hash<64, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, crp, cci, cval, err,
@@ -453,18 +490,6 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
     case kNumHash1024:
       run_warp_hash<1024, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, crp, cci, cval,
                              err, num_sms, s);
-      break;
-    case kNumRank2K:
-      run_warp_rank<2304, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
-                             cval, err, num_sms, s);
-      break;
-    case kNumRank4K:
-      run_warp_rank<4608, 8>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
-                             cval, err, num_sms, s);
-      break;
-    case kNumRank8K:
-      run_warp_rank<9216, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp, cci,
-                             cval, err, num_sms, s);
       break;
     case kNumHashBlock: {
       constexpr int NT = 512;

@@ -127,7 +127,8 @@ __global__ void __launch_bounds__(WPB * 32) sym_warp_kernel(const int* rows, con
 
 // Warp per row, bitmap over [lo, hi] (at most WORDS words), filled k-sequentially with
 // fire-and-forget atomicOr (no return value needed), then counted with one popcount pass.
-template <int WORDS, int WPB>
+// G lane groups share the warp (rows whose B rows are short; see walk.cuh).
+template <int WORDS, int WPB, int G>
 __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? 6 : 3) sym_warp_bitmap_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
     const int* lo_arr, const int* hi_arr, int* row_nnz, int* err) {
@@ -152,8 +153,9 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? 6 : 3) sym_warp_bitm
     }
     for (int w = lane; w < W; w += 32) bm[w] = 0u;
     __syncwarp();
-    const bool bad = fill_row_bitmap(A, B, A.rp[i], A.rp[i + 1], lo, (unsigned)span,
-                                     upper ? ig : 0, bm);
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    const int jmin = upper ? ig : 0;
+    const bool bad = fill_row_bitmap_g<G>(A, B, rs, re, lo, (unsigned)span, jmin, bm);
     __syncwarp();
     int cnt = 0;
     for (int w = lane; w < W; w += 32) cnt += __popc(bm[w]);
@@ -164,12 +166,12 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? 6 : 3) sym_warp_bitm
   }
 }
 
-template <int WORDS, int WPB>
-void launch_sym_bitmap(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
-                       int row_base, const int* lo, const int* hi, int* row_nnz, int* err,
-                       int num_sms, cudaStream_t s) {
+template <int WORDS, int WPB, int G>
+void launch_sym_bitmap_g(int bin, const int* rows, const long long* bin_off, Csr A, Csr B,
+                         int upper, int row_base, const int* lo, const int* hi, int* row_nnz,
+                         int* err, int num_sms, cudaStream_t s) {
   const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
-  auto kern = sym_warp_bitmap_kernel<WORDS, WPB>;
+  auto kern = sym_warp_bitmap_kernel<WORDS, WPB, G>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -180,6 +182,22 @@ void launch_sym_bitmap(int bin, const int* rows, const long long* bin_off, Csr A
   if (occ < 1) occ = 1;
   kern<<<num_sms * occ, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi,
                                               row_nnz, err);
+}
+
+// gidx: 0, 1, 2 for G = 1, 2, 4 lane groups.
+template <int WORDS, int WPB>
+void launch_sym_bitmap(int bin, int gidx, const int* rows, const long long* bin_off, Csr A,
+                       Csr B, int upper, int row_base, const int* lo, const int* hi, int* row_nnz,
+                       int* err, int num_sms, cudaStream_t s) {
+  if (gidx == 2)
+    launch_sym_bitmap_g<WORDS, WPB, 4>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz,
+                                       err, num_sms, s);
+  else if (gidx == 1)
+    launch_sym_bitmap_g<WORDS, WPB, 2>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz,
+                                       err, num_sms, s);
+  else
+    launch_sym_bitmap_g<WORDS, WPB, 1>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz,
+                                       err, num_sms, s);
 }
 
 // CTA per row. Bitmap windows of WB words (32*WB columns) over [lo, hi]; rows whose span exceeds
@@ -304,19 +322,22 @@ void launch_sym_warp(int bin, const int* rows, const long long* bin_off, Csr A, 
 void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
                      int row_base, const int* lo, const int* hi, const long long* flop,
                      int* row_nnz, int* err, int num_sms, cudaStream_t s) {
+  if (bin >= kSymBmS && bin < kSymBmM) {
+    launch_sym_bitmap<256, 8>(bin, bin - kSymBmS, rows, bin_off, A, B, upper, row_base, lo, hi,
+                              row_nnz, err, num_sms, s);
+    return;
+  }
+  if (bin >= kSymBmM && bin < kSymBmL) {
+    launch_sym_bitmap<1024, 8>(bin, bin - kSymBmM, rows, bin_off, A, B, upper, row_base, lo, hi,
+                               row_nnz, err, num_sms, s);
+    return;
+  }
+  if (bin >= kSymBmL && bin < kSymHashS) {
+    launch_sym_bitmap<4096, 4>(bin, bin - kSymBmL, rows, bin_off, A, B, upper, row_base, lo, hi,
+                               row_nnz, err, num_sms, s);
+    return;
+  }
   switch (bin) {
-    case kSymBmS:
-      launch_sym_bitmap<256, 8>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz, err,
-                                num_sms, s);
-      break;
-    case kSymBmM:
-      launch_sym_bitmap<1024, 8>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz, err,
-                                 num_sms, s);
-      break;
-    case kSymBmL:
-      launch_sym_bitmap<4096, 4>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz, err,
-                                 num_sms, s);
-      break;
     case kSymHashS:
       launch_sym_warp<256, 8>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop, row_nnz,
                               err, num_sms, s);

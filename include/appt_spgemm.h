@@ -143,7 +143,7 @@ typedef struct appt_csr_out {
   void *opaque;     /* owning handle; release with appt_free_out */
 } appt_csr_out;
 
-#define APPT_NUM_BINS 16
+#define APPT_NUM_BINS 32
 typedef struct appt_stats {
   int64_t products;                 /* intermediate products; flops = 2 * products */
   int64_t c_nnz;
@@ -177,6 +177,13 @@ int appt_free_out(appt_csr_out *C);
 
 /* CSR of A^T (rows sorted), device- or host-resident per in_mem/out_mem of opt. */
 int appt_transpose(const appt_csr *A, const appt_options *opt, appt_csr_out *AT);
+
+/* CSR of A^T written into caller-provided buffers in the operand format (int32 row_ptr):
+ * t_row_ptr has A->cols + 1 entries, t_col_idx / t_val A->nnz. Buffers are device or host per
+ * opt->in_mem (A and the outputs live in the same space). Counterpart of build_csc with an
+ * explicit column count and caller-owned outputs. */
+int appt_transpose_into(const appt_csr *A, const appt_options *opt, int32_t *t_row_ptr,
+                        int32_t *t_col_idx, double *t_val);
 
 /* Intermediate products per row of A*B (B = A when NULL); out has A->rows entries, host. */
 int appt_row_products(const appt_csr *A, const appt_csr *B, const appt_options *opt,

@@ -88,7 +88,7 @@ def tier_matrix():
 @pytest.mark.parametrize("method", ["adaptive", "hash", "merge"])
 def test_all_tiers(tier_matrix, method):
     C, st = check(tier_matrix, method=method)
-    used = {k for k, v in st["bin_rows"].items() if v > 0}
+    used = {k for k, v in st["tier_rows"].items() if v > 0}
     if method == "adaptive":
         assert {"rank2k", "hash64", "hash_block", "window"} <= used, used
     if method == "merge":
@@ -153,6 +153,20 @@ def test_invalid_column_is_an_error_not_a_fault():
         ap.spgemm(A)
     # the context is still usable afterwards
     check(M.random_csr(64, 64, 0.1, 3))
+
+
+def test_host_row_block_operand():
+    """A host row block (row_ptr not starting at 0, global col_idx/val) multiplies like the
+    corresponding rows of the full product."""
+    A = M.random_csr(500, 500, 0.03, 17, empty_rows=0.1)
+    r0, r1 = 137, 401
+    blk = M.Csr(r1 - r0, A.cols, A.row_ptr[r0:r1 + 1], A.col_idx, A.val)
+    C = ap.spgemm(blk, A)
+    R = oracle.spgemm(A)
+    lo, hi = int(R.row_ptr[r0]), int(R.row_ptr[r1])
+    assert np.array_equal(C.row_ptr, R.row_ptr[r0:r1 + 1] - lo)
+    assert np.array_equal(C.col_idx, R.col_idx[lo:hi])
+    assert np.array_equal(C.val, R.val[lo:hi])
 
 
 def test_uniform8_full():
