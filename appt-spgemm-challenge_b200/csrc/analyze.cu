@@ -10,6 +10,7 @@
 #include <climits>
 #include "common.cuh"
 #include "kernels.cuh"
+#include "walk.cuh"
 
 namespace appt {
 
@@ -19,7 +20,7 @@ constexpr int kAnThreads = 256;
 
 __device__ __forceinline__ int sym_bin_of(long long flop, long long span, long long rowlen) {
   if (flop == 0 || span <= 0) return 255;
-  const long long W = (span + 31) >> 5;
+  const long long W = span <= (1ll << 20) ? bitmap_words(span) : 1ll << 40;
   if (W <= 4096 && W <= 8 * flop + 64) {       // bitmap: clearing/counting W words pays off
     if (W <= 256) return kSymBmS + group_index(flop, rowlen);
     if (W <= 1024) return kSymBmM + group_index(flop, rowlen);
@@ -133,8 +134,8 @@ __device__ __forceinline__ int num_bin_of(int method, long long nnz, long long f
   if (nnz == 0) return 255;
   if (method == kMethodMerge && rowlen <= kMergeMaxLists) return kNumMerge;
   if (method == kMethodAdaptive) {
-    const long long W = (span + 31) >> 5;
-    const long long bytes = ((6 * W + 7) & ~7ll) + 10 * nnz;   // bitmap, prefix, sums, columns
+    // bitmap, prefix, sums and columns (plus one spare slot)
+    const long long bytes = span <= 65536 ? 6ll * bitmap_words(span) + 10 * (nnz + 1) : 1ll << 40;
     if (bytes <= 2304) return kNumRank2K + group_index(flop, rowlen);
     if (bytes <= 4608) return kNumRank4K + group_index(flop, rowlen);
     if (bytes <= 9216) return kNumRank8K + group_index(flop, rowlen);

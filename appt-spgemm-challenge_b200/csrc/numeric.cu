@@ -120,13 +120,14 @@ __global__ void __launch_bounds__(WPB * 32, 2048 / (WPB * 32) * 3 / 4) num_warp_
 // Row layout in the warp's shared budget: bitmap over [lo, hi] in 32-bit words (W words), a
 // 16-bit exclusive popcount prefix per word, the fp64 accumulator of the row's nnz entries and
 // the 16-bit column offset (j - lo) of every rank, so the finished row is copied out coalesced.
+// For the upper-triangle variants lo is already raised to the row's own index.
 // The bitmap is rebuilt from the products, after which the output position of column j is
 // prefix[w] + popcount(bitmap[w] & below(j)) -- values accumulate directly in output order, so
 // the row needs neither a hash table nor a sort. Products are visited k-sequentially (walk.cuh),
 // by G lane groups when the row's B rows are short: no atomics on the accumulator, and every sum
 // forms in the reference's order.
 #ifndef APPT_RANK_MIN_BLOCKS
-#define APPT_RANK_MIN_BLOCKS 5  // resident 256-thread CTAs per SM the register budget targets
+#define APPT_RANK_MIN_BLOCKS 4  // resident 256-thread CTAs per SM the register budget targets
 #endif
 template <int BUDGET, int WPB, int G>
 __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCKS : 7)
@@ -142,28 +143,36 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
   for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
        r += (long long)gridDim.x * WPB) {
     const int i = rows[b0 + r];
-    const int ig = i + row_base;
     const int lo = lo_arr[i];
     const long long span = (long long)hi_arr[i] - lo + 1;
     const int rs = A.rp[i], re = A.rp[i + 1];
     const long long c0 = crp[i];
     const int n = (int)(crp[i + 1] - c0);
-    const int W = (int)((span + 31) >> 5);
-    const int acc_off = ((6 * W) + 7) & ~7;
-    if (span <= 0 || span > 65536 || acc_off + 10 * n > BUDGET) {
+    if (span <= 0 || span > 65536) {
+      if (lane == 0) set_error(err, kErrCapacity);
+      continue;
+    }
+    const int W = bitmap_words(span);
+    const int acc_off = 6 * W;   // W is a multiple of 32
+    if (acc_off + 10 * (n + 1) > BUDGET) {
       if (lane == 0) set_error(err, kErrCapacity);
       continue;
     }
     unsigned* bm = reinterpret_cast<unsigned*>(base);
     unsigned short* pre = reinterpret_cast<unsigned short*>(base + 4 * W);
-    double* acc = reinterpret_cast<double*>(base + acc_off);
-    unsigned short* coff = reinterpret_cast<unsigned short*>(base + acc_off + 8 * n);
+    double* acc = reinterpret_cast<double*>(base + acc_off);              // n sums + spare
+    unsigned short* coff = reinterpret_cast<unsigned short*>(base + acc_off + 8 * (n + 1));
     for (int w = lane; w < W; w += 32) bm[w] = 0u;
     for (int t = lane; t < n; t += 32) acc[t] = 0.0;
     __syncwarp();
-    const int jmin = upper ? ig : 0;
+    // the first chunk of A entries stays in registers from the fill to the accumulation
+    int bs, len;
+    double a;
+    load_chunk(A, B, rs, re, bs, len, &a);
+    const int cnt = (re - rs) < 32 ? (re - rs) : 32;
     // 1) presence bitmap of the row's columns (native 32-bit shared atomicOr)
-    bool bad = fill_row_bitmap_g<G>(A, B, rs, re, lo, (unsigned)span, jmin, bm);
+    bool bad = fill_chunk_bitmap<G>(B, bs, len, cnt, lo, (unsigned)span, bm);
+    if (re - rs > 32) bad |= fill_row_bitmap_g<G>(A, B, rs + 32, re, lo, (unsigned)span, bm);
     __syncwarp();
     // 2) exclusive popcount prefix per word
     const int running = bitmap_prefix32(bm, W, pre);
@@ -171,7 +180,13 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     if (running != n) bad = true;
     // 3) accumulate at the column's rank, k by k; remember the column of every rank
     if (running == n) {
-      accumulate_row_ranked_g<G>(A, B, rs, re, lo, (unsigned)span, jmin, bm, pre, acc, coff);
+      accumulate_chunk_ranked<G>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre, acc, coff);
+      for (int cb = rs + 32; cb < re; cb += 32) {
+        load_chunk(A, B, cb, re, bs, len, &a);
+        const int c2 = (re - cb) < 32 ? (re - cb) : 32;
+        accumulate_chunk_ranked<G>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre, acc,
+                                   coff);
+      }
       // 4) the row is already in column order: one coalesced copy
       for (int t = lane; t < n; t += 32) {
         cci[c0 + t] = lo + (int)coff[t];

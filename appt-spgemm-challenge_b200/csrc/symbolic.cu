@@ -128,8 +128,12 @@ __global__ void __launch_bounds__(WPB * 32) sym_warp_kernel(const int* rows, con
 // Warp per row, bitmap over [lo, hi] (at most WORDS words), filled k-sequentially with
 // fire-and-forget atomicOr (no return value needed), then counted with one popcount pass.
 // G lane groups share the warp (rows whose B rows are short; see walk.cuh).
+#ifndef APPT_SYM_MIN_BLOCKS
+#define APPT_SYM_MIN_BLOCKS 5  // resident 256-thread CTAs per SM the register budget targets
+#endif
 template <int WORDS, int WPB, int G>
-__global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? 6 : 3) sym_warp_bitmap_kernel(
+__global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? APPT_SYM_MIN_BLOCKS : 3)
+    sym_warp_bitmap_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
     const int* lo_arr, const int* hi_arr, int* row_nnz, int* err) {
   extern __shared__ unsigned sym_smem[];
@@ -140,10 +144,9 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? 6 : 3) sym_warp_bitm
   for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
        r += (long long)gridDim.x * WPB) {
     const int i = rows[b0 + r];
-    const int ig = i + row_base;
     const int lo = lo_arr[i];
     const long long span = (long long)hi_arr[i] - lo + 1;
-    const int W = (int)((span + 31) >> 5);
+    const int W = span <= 32ll * WORDS ? bitmap_words(span) : WORDS + 1;
     if (span <= 0 || W > WORDS) {
       if (lane == 0) {
         set_error(err, kErrCapacity);
@@ -154,8 +157,7 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? 6 : 3) sym_warp_bitm
     for (int w = lane; w < W; w += 32) bm[w] = 0u;
     __syncwarp();
     const int rs = A.rp[i], re = A.rp[i + 1];
-    const int jmin = upper ? ig : 0;
-    const bool bad = fill_row_bitmap_g<G>(A, B, rs, re, lo, (unsigned)span, jmin, bm);
+    const bool bad = fill_row_bitmap_g<G>(A, B, rs, re, lo, (unsigned)span, bm);
     __syncwarp();
     int cnt = 0;
     for (int w = lane; w < W; w += 32) cnt += __popc(bm[w]);

@@ -83,155 +83,209 @@ __device__ __forceinline__ void walk_row_k_sequential(const Csr& A, const Csr& B
 }
 
 // ---------------------------------------------------------------------------------------------
-// Grouped walks for rows whose B rows are short. The warp is split into G groups of L = 32 / G
-// lanes; in step s group g takes A entry t = s * G + g of the current chunk and its lanes cover
-// that row of B (lane q of the group takes entries q, q + L, ...). Loads and rank computations
-// are shared by all groups; updates that must be ordered are applied group by group (G
-// sub-phases, each ended by __syncwarp), which keeps every column's contributions k-ascending.
+// Grouped walks for the bitmap tiers. The warp is split into G groups of L = 32 / G lanes; in
+// step s group g takes A entry t = s * G + g of the current chunk of 32 A entries and its lanes
+// cover that row of B (lane q of the group takes entries q, q + L, ...). The chunk's B row
+// bounds and A values sit in registers (one A entry per lane) and are broadcast by shuffles.
+// Lanes whose A entry lies past the row end hold an empty B row, so a step needs no bounds
+// test against the chunk size. When every B row of the chunk fits its group (the common case),
+// the loop body is branch-free: one predicated load per operand and one update.
 
-template <int G>
-__device__ __forceinline__ void load_group_entry(const Csr& B, int bs, int len, int cnt, int s,
-                                                 int grp, int sub, int& j, double* x) {
-  constexpr int L = 32 / G;
-  const int t = s * G + grp;
-  const int bt = __shfl_sync(kFull, bs, t & 31);
-  int lt = __shfl_sync(kFull, len, t & 31);
-  lt = t < cnt ? lt : 0;
-  j = -1;
-  if (sub < lt) {
-    j = __ldg(B.ci + bt + sub);
-    if (x) *x = __ldg(B.val + bt + sub);
+// Loads the chunk's A entries starting at `base`: B row start, length (0 past the row end) and,
+// when `a` is given, the A value.
+__device__ __forceinline__ void load_chunk(const Csr& A, const Csr& B, int base, int re, int& bs,
+                                           int& len, double* a) {
+  const int p = base + (threadIdx.x & 31);
+  bs = 0;
+  len = 0;
+  if (a) *a = 0.0;
+  if (p < re) {
+    const int k = __ldg(A.ci + p);
+    bs = __ldg(B.rp + k);
+    len = __ldg(B.rp + k + 1) - bs;
+    if (a) *a = __ldg(A.val + p);
   }
-  (void)L;
 }
 
-// Bitmap fill with G groups (order-free).
+// OR `bits` into the shared word at `p` when `pred` holds (fire-and-forget, no branch).
+__device__ __forceinline__ void red_or_shared_if(bool pred, unsigned* p, unsigned bits) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(p);
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q red.shared.or.b32 [%0], %1;\n\t}"
+      :: "r"(a), "r"(bits), "r"((int)pred) : "memory");
+}
+
+// Entry `sub` of the B row (bt, lt): its column (lo - 1, i.e. outside every span, when the row is
+// shorter) and, when `x` is given, its value. The load address is always valid (entry 0 of B for
+// lanes without an entry; B has entries whenever a row reaches these walks), so the load needs
+// no branch.
+__device__ __forceinline__ int load_b_entry(const Csr& B, int bt, int lt, int sub, int lo,
+                                            double* x) {
+  const bool v = sub < lt;
+  const int idx = v ? bt + sub : 0;
+  const int j = __ldg(B.ci + idx);
+  if (x) *x = __ldg(B.val + idx);
+  return v ? j : lo - 1;
+}
+
+// Bitmaps over a row's column span are stored with their 32-bit words permuted within blocks of
+// 32 (word w lives at swz(w)), so that words 32 * c apart -- the same bank in a plain layout,
+// e.g. the planes of a 3-D stencil -- fall into different banks. The word count is rounded up to
+// whole blocks (bitmap_words), which keeps the permutation inside the array.
+__host__ __device__ __forceinline__ unsigned swz(unsigned w) { return w ^ ((w >> 5) & 31u); }
+__host__ __device__ __forceinline__ int bitmap_words(long long span) {
+  return (int)((((span + 31) >> 5) + 31) & ~31ll);
+}
+
+// Presence bitmap of the row's columns: bit (j - lo) of logical word (j - lo) / 32 is set for
+// every product column j (order-free). The chunk's B row bounds are passed in (one A entry per lane). In the
+// common case the column indices of kFillBatch consecutive steps are loaded before any of them
+// is applied, so that many loads are in flight per warp; a batch that runs past the chunk wraps
+// to entries of the same chunk, which set bits that are set anyway. Returns true if a column
+// lies above the span (B rows not sorted); columns below lo are skipped (they are the ones the
+// upper-triangle variants drop).
+constexpr int kFillBatch = 8;
+
 template <int G>
-__device__ __forceinline__ bool fill_row_bitmap_g(const Csr& A, const Csr& B, int rs, int re,
-                                                  int lo, unsigned span, int jmin, unsigned* bm32) {
+__device__ __forceinline__ bool fill_chunk_bitmap(const Csr& B, int bs, int len, int cnt, int lo,
+                                                  unsigned span, unsigned* bm) {
   constexpr int L = 32 / G;
   const int lane = threadIdx.x & 31, grp = lane / L, sub = lane % L;
+  const int hi = lo + (int)span - 1;
   bool bad = false;
-  for (int base = rs; base < re; base += 32) {
-    const int p = base + lane;
-    const bool v = p < re;
-    const int k = v ? A.ci[p] : 0;
-    const int bs = v ? B.rp[k] : 0;
-    const int len = v ? B.rp[k + 1] - bs : 0;
-    const int cnt = (re - base) < 32 ? (re - base) : 32;
-    const bool any_long = __any_sync(kFull, len > L);
-    const int steps = (cnt + G - 1) / G;
-    int j0, j1, j2;
-    load_group_entry<G>(B, bs, len, cnt, 0, grp, sub, j0, nullptr);
-    load_group_entry<G>(B, bs, len, cnt, 1, grp, sub, j1, nullptr);
-    for (int s = 0; s < steps; ++s) {
-      load_group_entry<G>(B, bs, len, cnt, s + 2, grp, sub, j2, nullptr);
-      const unsigned off = (unsigned)(j0 - lo);
-      if (j0 >= jmin) {
-        if (off < span) atomicOr(bm32 + (off >> 5), 1u << (off & 31));
-        else bad = true;
+  if (!__any_sync(kFull, len > L)) {
+    for (int t0 = 0; t0 < cnt; t0 += G * kFillBatch) {
+      int jj[kFillBatch];
+#pragma unroll
+      for (int u = 0; u < kFillBatch; ++u) {
+        const int t = (t0 + u * G + grp) & 31;
+        jj[u] = load_b_entry(B, __shfl_sync(kFull, bs, t), __shfl_sync(kFull, len, t), sub, lo,
+                             nullptr);
       }
-      if (any_long) {
-        const int t = s * G + grp;
-        const int bt = __shfl_sync(kFull, bs, t & 31);
-        int lt = __shfl_sync(kFull, len, t & 31);
-        lt = t < cnt ? lt : 0;
-        for (int q = L + sub; q < lt; q += L) {
-          const int j = __ldg(B.ci + bt + q);
-          const unsigned o = (unsigned)(j - lo);
-          if (j >= jmin) {
-            if (o < span) atomicOr(bm32 + (o >> 5), 1u << (o & 31));
-            else bad = true;
-          }
-        }
+#pragma unroll
+      for (int u = 0; u < kFillBatch; ++u) {
+        const unsigned off = (unsigned)(jj[u] - lo);
+        red_or_shared_if(off < span, bm + swz(off >> 5), 1u << (off & 31));
+        bad |= jj[u] > hi;
       }
-      j0 = j1;
-      j1 = j2;
+    }
+  } else {
+    for (int t0 = 0; t0 < cnt; t0 += G) {
+      const int t = t0 + grp;
+      const int bt = __shfl_sync(kFull, bs, t);
+      const int lt = __shfl_sync(kFull, len, t);
+      for (int q = sub; q < lt; q += L) {
+        const int j = __ldg(B.ci + bt + q);
+        const unsigned off = (unsigned)(j - lo);
+        red_or_shared_if(off < span, bm + swz(off >> 5), 1u << (off & 31));
+        bad |= j > hi;
+      }
     }
   }
   return bad;
 }
 
-// Exclusive popcount prefix of W 32-bit bitmap words into 16-bit entries; returns the total.
+template <int G>
+__device__ __forceinline__ bool fill_row_bitmap_g(const Csr& A, const Csr& B, int rs, int re,
+                                                  int lo, unsigned span, unsigned* bm) {
+  bool bad = false;
+  for (int base = rs; base < re; base += 32) {
+    int bs, len;
+    load_chunk(A, B, base, re, bs, len, nullptr);
+    const int cnt = (re - base) < 32 ? (re - base) : 32;
+    bad |= fill_chunk_bitmap<G>(B, bs, len, cnt, lo, span, bm);
+  }
+  return bad;
+}
+
+// Exclusive popcount prefix of the W (a multiple of 32) permuted bitmap words, in logical word
+// order, into 16-bit entries stored at the same permuted positions (each lane owns a contiguous
+// run of logical words); returns the total number of set bits.
 __device__ __forceinline__ int bitmap_prefix32(const unsigned* bm, int W, unsigned short* pre) {
   const int lane = threadIdx.x & 31;
-  const int per = (W + 31) >> 5;
-  const int w0 = lane * per;
-  const int w1 = (w0 + per < W) ? w0 + per : W;
+  const int per = W >> 5;
+  const unsigned w0 = lane * per;
   int s = 0;
-  for (int w = w0; w < w1; ++w) s += __popc(bm[w]);
+  for (int q = 0; q < per; ++q) s += __popc(bm[swz(w0 + q)]);
   const int incl = warp_incl_scan(s);
   int run = incl - s;
-  for (int w = w0; w < w1; ++w) {
+  for (int q = 0; q < per; ++q) {
+    const unsigned w = swz(w0 + q);
     pre[w] = (unsigned short)run;
     run += __popc(bm[w]);
   }
   return __shfl_sync(kFull, incl, 31);
 }
 
-// Ranked accumulation with G groups: acc[rank(j)] += a_ik * b_kj and coff[rank(j)] = j - lo,
-// with rank(j) = pre[w] + popc(bm[w] below j) over 32-bit words. Sums form k-ascending.
+// Rank of span offset `off` among the set bits, or `dummy` when off is outside the span (word 0
+// is read instead, so the lookup needs no branch).
+__device__ __forceinline__ int rank_or(const unsigned* bm, const unsigned short* pre, unsigned off,
+                                       unsigned span, int dummy) {
+  const bool ok = off < span;
+  const unsigned w = ok ? swz(off >> 5) : 0u;
+  const int r = (int)pre[w] + __popc(bm[w] & ((1u << (off & 31)) - 1u));
+  return ok ? r : dummy;
+}
+
+// Ranked accumulation over one chunk of A entries: acc[rank(j)] += a_ik * b_kj and
+// coff[rank(j)] = j - lo for every product with j in the span, k-sequentially (G ordered
+// sub-phases per step when G > 1). Lanes without a product in a (sub-)phase update the spare
+// slot acc[n] / coff[n] instead, so the step has no branch. In the common case the B entries of
+// the next two steps are loaded while the current step is applied.
 template <int G>
-__device__ __forceinline__ void accumulate_row_ranked_g(const Csr& A, const Csr& B, int rs, int re,
-                                                        int lo, unsigned span, int jmin,
+__device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, int len, double a,
+                                                        int cnt, int lo, unsigned span, int n,
                                                         const unsigned* bm,
                                                         const unsigned short* pre, double* acc,
                                                         unsigned short* coff) {
   constexpr int L = 32 / G;
   const int lane = threadIdx.x & 31, grp = lane / L, sub = lane % L;
-  for (int base = rs; base < re; base += 32) {
-    const int p = base + lane;
-    const bool v = p < re;
-    const int k = v ? A.ci[p] : 0;
-    const int bs = v ? B.rp[k] : 0;
-    const int len = v ? B.rp[k + 1] - bs : 0;
-    const double a = v ? A.val[p] : 0.0;
-    const int cnt = (re - base) < 32 ? (re - base) : 32;
-    const bool any_long = __any_sync(kFull, len > L);
-    const int steps = (cnt + G - 1) / G;
-    int j0, j1, j2;
-    double x0, x1, x2;
-    load_group_entry<G>(B, bs, len, cnt, 0, grp, sub, j0, &x0);
-    load_group_entry<G>(B, bs, len, cnt, 1, grp, sub, j1, &x1);
-    for (int s = 0; s < steps; ++s) {
-      load_group_entry<G>(B, bs, len, cnt, s + 2, grp, sub, j2, &x2);
-      const int t = s * G + grp;
-      const double at = __shfl_sync(kFull, a, t & 31);
+  if (!__any_sync(kFull, len > L)) {
+    double x0, x1;
+    int j0 = load_b_entry(B, __shfl_sync(kFull, bs, grp), __shfl_sync(kFull, len, grp), sub, lo,
+                          &x0);
+    int j1 = load_b_entry(B, __shfl_sync(kFull, bs, G + grp), __shfl_sync(kFull, len, G + grp),
+                          sub, lo, &x1);
+    for (int t0 = 0; t0 < cnt; t0 += G) {
+      // entries two steps ahead (a step past the chunk reads a valid row and is discarded)
+      const int t2 = (t0 + 2 * G + grp) & 31;
+      double x2;
+      const int j2 = load_b_entry(B, __shfl_sync(kFull, bs, t2), __shfl_sync(kFull, len, t2),
+                                  sub, lo, &x2);
+      const double at = __shfl_sync(kFull, a, t0 + grp);
       const unsigned off = (unsigned)(j0 - lo);
-      const bool ok = j0 >= jmin && off < span;
-      int pos = 0;
-      if (ok) pos = pre[off >> 5] + __popc(bm[off >> 5] & ((1u << (off & 31)) - 1u));
-      int lt = 0, bt = 0;
-      if (any_long) {
-        bt = __shfl_sync(kFull, bs, t & 31);
-        lt = __shfl_sync(kFull, len, t & 31);
-        lt = t < cnt ? lt : 0;
-      }
+      const int r = rank_or(bm, pre, off, span, n);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        if (grp == g) {
-          if (ok) {
-            acc[pos] = mul_add_rn(acc[pos], at, x0);
-            coff[pos] = (unsigned short)off;
-          }
-          if (any_long) {
-            for (int q = L + sub; q < lt; q += L) {
-              const int j = __ldg(B.ci + bt + q);
-              const unsigned o = (unsigned)(j - lo);
-              if (j >= jmin && o < span) {
-                const int ps = pre[o >> 5] + __popc(bm[o >> 5] & ((1u << (o & 31)) - 1u));
-                acc[ps] = mul_add_rn(acc[ps], at, __ldg(B.val + bt + q));
-                coff[ps] = (unsigned short)o;
-              }
-            }
-          }
-        }
+        const int pos = (G == 1 || grp == g) ? r : n;
+        acc[pos] = mul_add_rn(acc[pos], at, x0);
+        coff[pos] = (unsigned short)off;
         __syncwarp();
       }
       j0 = j1;
       x0 = x1;
       j1 = j2;
       x1 = x2;
+    }
+  } else {
+    for (int t0 = 0; t0 < cnt; t0 += G) {
+      const int t = t0 + grp;
+      const int bt = __shfl_sync(kFull, bs, t);
+      const int lt = __shfl_sync(kFull, len, t);
+      const double at = __shfl_sync(kFull, a, t);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        if (G == 1 || grp == g) {
+          for (int q = sub; q < lt; q += L) {
+            const int j = __ldg(B.ci + bt + q);
+            const unsigned off = (unsigned)(j - lo);
+            const int pos = rank_or(bm, pre, off, span, n);
+            acc[pos] = mul_add_rn(acc[pos], at, __ldg(B.val + bt + q));
+            coff[pos] = (unsigned short)off;
+          }
+        }
+        __syncwarp();
+      }
     }
   }
 }
