@@ -39,8 +39,8 @@ template <int LPR>
 __global__ void __launch_bounds__(kAnThreads) analyze_kernel(Csr A, Csr B, int upper, int row_base,
                                                              int method, long long* flop, int* lo_out,
                                                              int* hi_out, uint8_t* symkey,
-                                                             int* row_nnz, AnalyzeStats* stats,
-                                                             int* err) {
+                                                             int* row_nnz,
+                                                             AnalyzeStats* stats, int* err) {
   constexpr int RPW = 32 / LPR;
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR, grp = lane / LPR;

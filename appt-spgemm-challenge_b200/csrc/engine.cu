@@ -63,6 +63,10 @@ struct DeviceCtx {
   cudaStream_t stream = nullptr;
   cudaMemPool_t pool = nullptr;
   char* stage = nullptr;   // pinned host staging for small device->host reads
+  // bitmap handoff arena (symbolic -> numeric rank tier), allocated on first use and kept: calls
+  // on a device are serialised by `mu` and each ends with its work complete
+  unsigned* harena = nullptr;
+  bool harena_tried = false;
   std::mutex mu;
   bool ok = false;
 };
@@ -324,9 +328,11 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   uint8_t* symkey = sc.get<uint8_t>(m);
   uint8_t* numkey = sc.get<uint8_t>(m);
   int* row_nnz = sc.get<int>(m);
+  int* hslot = sc.get<int>(m);
   int* rows_sym = sc.get<int>(m);
   int* rows_num = sc.get<int>(m);
   long long* crp = sc.get<long long>((size_t)m + 1);
+  unsigned long long* htop = sc.get<unsigned long long>(1);
   long long* boff_sym = sc.get<long long>(kMaxBins + 1);
   long long* boff_num = sc.get<long long>(kMaxBins + 1);
   AnalyzeStats* gst = sc.get<AnalyzeStats>(1);
@@ -339,6 +345,26 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   }
   CK(cudaMemsetAsync(gst, 0, sizeof(AnalyzeStats), s));
   CK(cudaMemsetAsync(err, 0, sizeof(int) * 4, s));
+  CK(cudaMemsetAsync(htop, 0, sizeof(unsigned long long), s));
+  CK(cudaMemsetAsync(hslot, 0xff, sizeof(int) * (size_t)m, s));
+
+  // arena for the bitmaps the symbolic bitmap tier hands to the numeric rank tier (rows that
+  // find it full rebuild their bitmaps in the numeric phase)
+  if (!ctx->harena_tried) {
+    ctx->harena_tried = true;
+    if (cudaMalloc((void**)&ctx->harena, sizeof(unsigned) * (size_t)kHandoffArenaWords) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      ctx->harena = nullptr;
+    }
+  }
+  RowBitmaps handoff;
+  if (ctx->harena && m > 0) {
+    handoff.slot = hslot;
+    handoff.data = ctx->harena;
+    handoff.top = htop;
+    handoff.capacity = kHandoffArenaWords;
+  }
 
   tm.begin(kPhAnalyze);
   launch_analyze(A, B, upper, row_base, method, lanes_per_row(a_nnz, m), flop, lo, hi, symkey,
@@ -349,8 +375,8 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   tm.begin(kPhSymbolic);
   if (m > 0) {
     for (int b = 0; b < kNumSymBins; ++b)
-      launch_symbolic(b, rows_sym, boff_sym, A, B, upper, row_base, lo, hi, flop, row_nnz, err,
-                      sms, s);
+      launch_symbolic(b, rows_sym, boff_sym, A, B, upper, row_base, lo, hi, flop, row_nnz, handoff,
+                      err, sms, s);
     note_launches(kNumSymBins);
     if (method == kMethodMerge) {
       launch_merge_count(rows_sym, boff_sym, kSymMergeBin, A, B, upper, row_base, row_nnz, err,
@@ -407,8 +433,8 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
       launch_merge_numeric(rows_num, boff_num, b, nr, A, B, upper, row_base, crp, cci, cval, err,
                            sms, s);
     else
-      launch_numeric(b, rows_num, boff_num, nr, A, B, upper, row_base, lo, hi, flop, crp, cci, cval,
-                     err, sms, s);
+      launch_numeric(b, rows_num, boff_num, nr, A, B, upper, row_base, lo, hi, flop, handoff, crp,
+                     cci, cval, err, sms, s);
     note_launches(1);
   }
   tm.end();

@@ -14,6 +14,34 @@ constexpr int kWindowCols = 16384;      // CTA window tier: columns per window
 constexpr int kHashBlockSlots = 8192;   // CTA hash tier: table slots (rows with nnz <= slots/2)
 constexpr int kSymBlockWords = 32768;   // CTA symbolic bitmap window: 2^20 columns
 constexpr int kMergeMaxLists = 256;     // merge tier: rows with more A entries use other tiers
+constexpr int kRankMaxBudget = 9216;    // largest per-warp shared budget of the rank tier (bytes)
+
+// Column bitmaps that the symbolic bitmap tier hands to the rank tier of the numeric phase, so
+// that the numeric phase need not walk the products twice. The bitmaps live in one arena of
+// `capacity` words; each warp of the symbolic kernel takes chunks of it with one atomic on `top`
+// and places its rows' bitmaps there (logical word order). slot[i] = first word of row i's bitmap
+// / 32, or -1 (no bitmap: the arena was full, the row does not qualify, or it ran in another
+// tier). Only rows that could fit the rank tier and whose products repeat columns enough
+// (handoff_pays) are handed off. data == nullptr: no handoff at all.
+struct RowBitmaps {
+  int* slot = nullptr;
+  unsigned* data = nullptr;
+  unsigned long long* top = nullptr;
+  long long capacity = 0;
+};
+
+constexpr int kHandoffChunkWords = 16384;          // arena words a warp takes at a time
+constexpr long long kHandoffArenaWords = 1ll << 28;  // arena size (1 GiB)
+
+__host__ __device__ __forceinline__ bool handoff_fits_rank(int bitmap_words) {
+  return 6ll * bitmap_words + 20 <= kRankMaxBudget;
+}
+
+// The handoff replaces one pass over the row's products by a copy of its bitmap; it pays when
+// the products repeat columns (at least twice as many products as distinct columns).
+__host__ __device__ __forceinline__ bool handoff_pays(long long flop, long long nnz) {
+  return flop >= 2 * nnz;
+}
 
 // Lane groups of the warp walks (walk.cuh): a row whose B rows average <= 8 entries is walked by
 // 4 groups of 8 lanes, <= 16 by 2 groups of 16, longer by the whole warp. Tiers that walk
@@ -88,13 +116,13 @@ void launch_classify_numeric(Csr A, int m, int method, const long long* flop, co
 // symbolic.cu
 void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
                      int row_base, const int* lo, const int* hi, const long long* flop,
-                     int* row_nnz, int* err, int num_sms, cudaStream_t s);
+                     int* row_nnz, RowBitmaps handoff, int* err, int num_sms, cudaStream_t s);
 
 // numeric.cu
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows_host,
                     Csr A, Csr B, int upper, int row_base, const int* lo, const int* hi,
-                    const long long* flop, const long long* crp, int* cci, double* cval, int* err, int num_sms,
-                    cudaStream_t s);
+                    const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
+                    double* cval, int* err, int num_sms, cudaStream_t s);
 
 // merge.cu
 void launch_merge_count(const int* rows, const long long* bin_off, int bin, Csr A, Csr B,

@@ -168,7 +168,8 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
   partition_rows(symkey, m, kNumSymBins + 1, rows_sym, boff_sym, pscr, s);
   if (m > 0)
     for (int b = 0; b < kNumSymBins; ++b)
-      launch_symbolic(b, rows_sym, boff_sym, dA, dB, 0, 0, lo, hi, flop, row_nnz, err, sms, s);
+      launch_symbolic(b, rows_sym, boff_sym, dA, dB, 0, 0, lo, hi, flop, row_nnz, RowBitmaps{}, err,
+                      sms, s);
   scan_exclusive(row_nnz, crp, m, scs, s);
   launch_classify_numeric(dA, m, kMethodAdaptive, flop, lo, hi, row_nnz, numkey, sms, s);
   partition_rows(numkey, m, kNumNumBins, rows_num, boff_num, pscr, s);
@@ -205,8 +206,8 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
   for (int b = 0; b < kNumNumBins; ++b) {
     const long long nr = boff[b + 1] - boff[b];
     if (nr <= 0) continue;
-    launch_numeric(b, rows_num, boff_num, nr, dA, dB, 0, 0, lo, hi, flop, crp, cci, cval, err, sms,
-                   s);
+    launch_numeric(b, rows_num, boff_num, nr, dA, dB, 0, 0, lo, hi, flop, RowBitmaps{}, crp, cci, cval,
+                   err, sms, s);
     note_launches(1);
   }
   e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s);

@@ -133,8 +133,8 @@ template <int BUDGET, int WPB, int G>
 __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCKS : 7)
     num_warp_rank_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
-    const int* lo_arr, const int* hi_arr, const long long* crp, int* cci, double* cval,
-    int* err) {
+    const int* lo_arr, const int* hi_arr, RowBitmaps handoff, const long long* crp, int* cci,
+    double* cval, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned char* base = num_smem + (size_t)warp * BUDGET;
@@ -162,30 +162,42 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     unsigned short* pre = reinterpret_cast<unsigned short*>(base + 4 * W);
     double* acc = reinterpret_cast<double*>(base + acc_off);              // n sums + spare
     unsigned short* coff = reinterpret_cast<unsigned short*>(base + acc_off + 8 * (n + 1));
-    for (int w = lane; w < W; w += 32) bm[w] = 0u;
+    const unsigned* hbm = nullptr;   // the symbolic phase's bitmap of this row, if handed off
+    if (handoff.data) {
+      const int hs = handoff.slot[i];
+      if (hs >= 0) hbm = handoff.data + 32ll * hs;
+    }
     for (int t = lane; t < n; t += 32) acc[t] = 0.0;
-    __syncwarp();
-    // the first chunk of A entries stays in registers from the fill to the accumulation
+    // the first chunk of A entries stays in registers
     int bs, len;
     double a;
     load_chunk(A, B, rs, re, bs, len, &a);
     const int cnt = (re - rs) < 32 ? (re - rs) : 32;
-    // 1) presence bitmap of the row's columns (native 32-bit shared atomicOr)
-    bool bad = fill_chunk_bitmap<G>(B, bs, len, cnt, lo, (unsigned)span, bm);
-    if (re - rs > 32) bad |= fill_row_bitmap_g<G>(A, B, rs + 32, re, lo, (unsigned)span, bm);
-    __syncwarp();
+    bool bad = false;
+    // 1) presence bitmap of the row's columns: copied in, or built from the products
+    if (hbm) {
+      for (int w = lane; w < W; w += 32) bm[swz(w)] = __ldg(hbm + w);
+      __syncwarp();
+    } else {
+      for (int w = lane; w < W; w += 32) bm[w] = 0u;
+      __syncwarp();
+      bad = fill_chunk_bitmap<G>(B, bs, len, cnt, lo, (unsigned)span, bm);
+      if (re - rs > 32) bad |= fill_row_bitmap_g<G>(A, B, rs + 32, re, lo, (unsigned)span, bm);
+      __syncwarp();
+    }
     // 2) exclusive popcount prefix per word
     const int running = bitmap_prefix32(bm, W, pre);
     __syncwarp();
     if (running != n) bad = true;
     // 3) accumulate at the column's rank, k by k; remember the column of every rank
     if (running == n) {
-      accumulate_chunk_ranked<G>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre, acc, coff);
+      accumulate_chunk_ranked<G>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre, acc,
+                                       coff);
       for (int cb = rs + 32; cb < re; cb += 32) {
         load_chunk(A, B, cb, re, bs, len, &a);
         const int c2 = (re - cb) < 32 ? (re - cb) : 32;
         accumulate_chunk_ranked<G>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre, acc,
-                                   coff);
+                                         coff);
       }
       // 4) the row is already in column order: one coalesced copy
       for (int t = lane; t < n; t += 32) {
@@ -431,8 +443,8 @@ void run_warp_hash(int bin, const int* rows, const long long* bin_off, long long
 template <int BUDGET, int WPB, int G>
 void run_warp_rank_g(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
                      Csr B, int upper, int row_base, const int* lo, const int* hi,
-                     const long long* crp, int* cci, double* cval, int* err, int num_sms,
-                     cudaStream_t s) {
+                     const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
+                     double* cval, int* err, int num_sms, cudaStream_t s) {
   const size_t smem = (size_t)WPB * BUDGET;
   auto kern = num_warp_rank_kernel<BUDGET, WPB, G>;
   static bool attr = false;
@@ -441,48 +453,47 @@ void run_warp_rank_g(int bin, const int* rows, const long long* bin_off, long lo
     attr = true;
   }
   const int grid = occupancy_grid(kern, WPB * 32, smem, num_sms, nrows, WPB);
-  kern<<<grid, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, crp, cci,
-                                    cval, err);
+  kern<<<grid, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, handoff,
+                                    crp, cci, cval, err);
 }
 
 // bin = tier base + group index (0, 1, 2 for G = 1, 2, 4)
 template <int BUDGET, int WPB>
 void run_warp_rank(int bin, int gidx, const int* rows, const long long* bin_off, long long nrows,
                    Csr A, Csr B, int upper, int row_base, const int* lo, const int* hi,
-                   const long long* crp, int* cci, double* cval, int* err, int num_sms,
-                   cudaStream_t s) {
+                   const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
+                   double* cval, int* err, int num_sms, cudaStream_t s) {
   if (gidx == 2)
-    run_warp_rank_g<BUDGET, WPB, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp,
-                                    cci, cval, err, num_sms, s);
+    run_warp_rank_g<BUDGET, WPB, 4>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi,
+                                    flop, handoff, crp, cci, cval, err, num_sms, s);
   else if (gidx == 1)
-    run_warp_rank_g<BUDGET, WPB, 2>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp,
-                                    cci, cval, err, num_sms, s);
+    run_warp_rank_g<BUDGET, WPB, 2>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi,
+                                    flop, handoff, crp, cci, cval, err, num_sms, s);
   else
-    run_warp_rank_g<BUDGET, WPB, 1>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi, crp,
-                                    cci, cval, err, num_sms, s);
+    run_warp_rank_g<BUDGET, WPB, 1>(bin, rows, bin_off, nrows, A, B, upper, row_base, lo, hi,
+                                    flop, handoff, crp, cci, cval, err, num_sms, s);
 }
 
 }  // namespace
 
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
                     Csr B, int upper, int row_base, const int* lo, const int* hi,
-                    const long long* flop, const long long* crp, int* cci, double* cval, int* err, int num_sms,
-                    cudaStream_t s) {
+                    const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
+                    double* cval, int* err, int num_sms, cudaStream_t s) {
   if (nrows <= 0) return;
-  (void)flop;
   if (bin >= kNumRank2K && bin < kNumRank2K + 3) {
     run_warp_rank<2304, 8>(bin, bin - kNumRank2K, rows, bin_off, nrows, A, B, upper, row_base, lo,
-                           hi, crp, cci, cval, err, num_sms, s);
+                           hi, flop, handoff, crp, cci, cval, err, num_sms, s);
     return;
   }
   if (bin >= kNumRank4K && bin < kNumRank4K + 3) {
     run_warp_rank<4608, 8>(bin, bin - kNumRank4K, rows, bin_off, nrows, A, B, upper, row_base, lo,
-                           hi, crp, cci, cval, err, num_sms, s);
+                           hi, flop, handoff, crp, cci, cval, err, num_sms, s);
     return;
   }
   if (bin >= kNumRank8K && bin < kNumRank8K + 3) {
     run_warp_rank<9216, 4>(bin, bin - kNumRank8K, rows, bin_off, nrows, A, B, upper, row_base, lo,
-                           hi, crp, cci, cval, err, num_sms, s);
+                           hi, flop, handoff, crp, cci, cval, err, num_sms, s);
     return;
   }
   switch (bin) {

@@ -125,27 +125,32 @@ __global__ void __launch_bounds__(WPB * 32) sym_warp_kernel(const int* rows, con
   }
 }
 
-// Warp per row, bitmap over [lo, hi] (at most WORDS words), filled k-sequentially with
-// fire-and-forget atomicOr (no return value needed), then counted with one popcount pass.
-// G lane groups share the warp (rows whose B rows are short; see walk.cuh).
+// Warp per row, bitmap over [lo, hi] (at most WORDS words), filled with fire-and-forget shared
+// OR operations, then counted. G lane groups share the warp (rows whose B rows are short; see
+// walk.cuh). Rows that could fit the rank tier and whose products repeat columns enough
+// (handoff_pays) also copy the finished bitmap out (coalesced, logical word order) into the
+// handoff arena, in chunks the warp takes with one atomic each, for the numeric rank tier.
 #ifndef APPT_SYM_MIN_BLOCKS
 #define APPT_SYM_MIN_BLOCKS 5  // resident 256-thread CTAs per SM the register budget targets
 #endif
 template <int WORDS, int WPB, int G>
 __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? APPT_SYM_MIN_BLOCKS : 3)
-    sym_warp_bitmap_kernel(
-    const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
-    const int* lo_arr, const int* hi_arr, int* row_nnz, int* err) {
+    sym_warp_bitmap_kernel(const int* rows, const long long* bin_off, int bin, Csr A, Csr B,
+                           int upper, int row_base, const int* lo_arr, const int* hi_arr,
+                           const long long* flop_arr, int* row_nnz, RowBitmaps handoff,
+                           int* err) {
   extern __shared__ unsigned sym_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned* bm = sym_smem + warp * WORDS;
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
+  long long chunk_cur = 0, chunk_end = 0;   // this warp's piece of the handoff arena
   for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
        r += (long long)gridDim.x * WPB) {
     const int i = rows[b0 + r];
     const int lo = lo_arr[i];
     const long long span = (long long)hi_arr[i] - lo + 1;
+    const long long flop = flop_arr[i];
     const int W = span <= 32ll * WORDS ? bitmap_words(span) : WORDS + 1;
     if (span <= 0 || W > WORDS) {
       if (lane == 0) {
@@ -164,14 +169,31 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? APPT_SYM_MIN_BLOCKS 
     cnt = warp_sum(cnt);
     if (__any_sync(kFull, bad) && lane == 0) set_error(err, kErrCapacity);
     if (lane == 0) row_nnz[i] = cnt;
+    if (handoff.data && handoff_fits_rank(W) && handoff_pays(flop, cnt)) {
+      if (chunk_cur + W > chunk_end) {
+        unsigned long long c = 0;
+        if (lane == 0) c = atomicAdd(handoff.top, (unsigned long long)kHandoffChunkWords);
+        c = __shfl_sync(kFull, c, 0);
+        chunk_cur = (long long)c;
+        chunk_end = chunk_cur + kHandoffChunkWords;
+        if (chunk_end > handoff.capacity) chunk_end = chunk_cur;   // arena exhausted
+      }
+      if (chunk_cur + W <= chunk_end) {
+        unsigned* out = handoff.data + chunk_cur;
+        for (int w = lane; w < W; w += 32) out[w] = bm[swz(w)];
+        if (lane == 0) handoff.slot[i] = (int)(chunk_cur >> 5);
+        chunk_cur += W;
+      }
+    }
     __syncwarp();
   }
 }
 
 template <int WORDS, int WPB, int G>
 void launch_sym_bitmap_g(int bin, const int* rows, const long long* bin_off, Csr A, Csr B,
-                         int upper, int row_base, const int* lo, const int* hi, int* row_nnz,
-                         int* err, int num_sms, cudaStream_t s) {
+                         int upper, int row_base, const int* lo, const int* hi,
+                         const long long* flop, int* row_nnz, RowBitmaps handoff, int* err,
+                         int num_sms, cudaStream_t s) {
   const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
   auto kern = sym_warp_bitmap_kernel<WORDS, WPB, G>;
   static bool attr_set = false;
@@ -183,23 +205,24 @@ void launch_sym_bitmap_g(int bin, const int* rows, const long long* bin_off, Csr
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, WPB * 32, smem);
   if (occ < 1) occ = 1;
   kern<<<num_sms * occ, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi,
-                                              row_nnz, err);
+                                              flop, row_nnz, handoff, err);
 }
 
 // gidx: 0, 1, 2 for G = 1, 2, 4 lane groups.
 template <int WORDS, int WPB>
 void launch_sym_bitmap(int bin, int gidx, const int* rows, const long long* bin_off, Csr A,
-                       Csr B, int upper, int row_base, const int* lo, const int* hi, int* row_nnz,
-                       int* err, int num_sms, cudaStream_t s) {
+                       Csr B, int upper, int row_base, const int* lo, const int* hi,
+                       const long long* flop, int* row_nnz, RowBitmaps handoff, int* err,
+                       int num_sms, cudaStream_t s) {
   if (gidx == 2)
-    launch_sym_bitmap_g<WORDS, WPB, 4>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz,
-                                       err, num_sms, s);
+    launch_sym_bitmap_g<WORDS, WPB, 4>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop,
+                                       row_nnz, handoff, err, num_sms, s);
   else if (gidx == 1)
-    launch_sym_bitmap_g<WORDS, WPB, 2>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz,
-                                       err, num_sms, s);
+    launch_sym_bitmap_g<WORDS, WPB, 2>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop,
+                                       row_nnz, handoff, err, num_sms, s);
   else
-    launch_sym_bitmap_g<WORDS, WPB, 1>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, row_nnz,
-                                       err, num_sms, s);
+    launch_sym_bitmap_g<WORDS, WPB, 1>(bin, rows, bin_off, A, B, upper, row_base, lo, hi, flop,
+                                       row_nnz, handoff, err, num_sms, s);
 }
 
 // CTA per row. Bitmap windows of WB words (32*WB columns) over [lo, hi]; rows whose span exceeds
@@ -323,20 +346,20 @@ void launch_sym_warp(int bin, const int* rows, const long long* bin_off, Csr A, 
 
 void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
                      int row_base, const int* lo, const int* hi, const long long* flop,
-                     int* row_nnz, int* err, int num_sms, cudaStream_t s) {
+                     int* row_nnz, RowBitmaps handoff, int* err, int num_sms, cudaStream_t s) {
   if (bin >= kSymBmS && bin < kSymBmM) {
     launch_sym_bitmap<256, 8>(bin, bin - kSymBmS, rows, bin_off, A, B, upper, row_base, lo, hi,
-                              row_nnz, err, num_sms, s);
+                              flop, row_nnz, handoff, err, num_sms, s);
     return;
   }
   if (bin >= kSymBmM && bin < kSymBmL) {
     launch_sym_bitmap<1024, 8>(bin, bin - kSymBmM, rows, bin_off, A, B, upper, row_base, lo, hi,
-                               row_nnz, err, num_sms, s);
+                               flop, row_nnz, handoff, err, num_sms, s);
     return;
   }
   if (bin >= kSymBmL && bin < kSymHashS) {
     launch_sym_bitmap<4096, 4>(bin, bin - kSymBmL, rows, bin_off, A, B, upper, row_base, lo, hi,
-                               row_nnz, err, num_sms, s);
+                               flop, row_nnz, handoff, err, num_sms, s);
     return;
   }
   switch (bin) {

@@ -217,21 +217,22 @@ __device__ __forceinline__ int bitmap_prefix32(const unsigned* bm, int W, unsign
   return __shfl_sync(kFull, incl, 31);
 }
 
-// Rank of span offset `off` among the set bits, or `dummy` when off is outside the span (word 0
-// is read instead, so the lookup needs no branch).
+// Rank of span offset `off` among the set bits, or `dummy` (the row's nnz, the spare slot) when
+// off is outside the span (word 0 is read instead, so the lookup needs no branch). The result
+// never exceeds `dummy`, whatever the bitmap holds.
 __device__ __forceinline__ int rank_or(const unsigned* bm, const unsigned short* pre, unsigned off,
                                        unsigned span, int dummy) {
   const bool ok = off < span;
   const unsigned w = ok ? swz(off >> 5) : 0u;
   const int r = (int)pre[w] + __popc(bm[w] & ((1u << (off & 31)) - 1u));
-  return ok ? r : dummy;
+  return ok ? min(r, dummy) : dummy;
 }
 
 // Ranked accumulation over one chunk of A entries: acc[rank(j)] += a_ik * b_kj and
 // coff[rank(j)] = j - lo for every product with j in the span, k-sequentially (G ordered
-// sub-phases per step when G > 1). Lanes without a product in a (sub-)phase update the spare
-// slot acc[n] / coff[n] instead, so the step has no branch. In the common case the B entries of
-// the next two steps are loaded while the current step is applied.
+// sub-phases per step when G > 1). Lanes without a product in a (sub-)phase update the
+// spare slot acc[n] / coff[n] instead, so the step has no branch. In the common case the B
+// entries of the next two steps are loaded while the current step is applied.
 template <int G>
 __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, int len, double a,
                                                         int cnt, int lo, unsigned span, int n,
