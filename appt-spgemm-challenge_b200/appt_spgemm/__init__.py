@@ -34,7 +34,7 @@ NUM_BINS = 32
 # per warp, chosen by the average length of the row's B rows).
 BIN_NAMES = ["rank2k_g1", "rank2k_g2", "rank2k_g4", "rank4k_g1", "rank4k_g2", "rank4k_g4",
              "rank8k_g1", "rank8k_g2", "rank8k_g4", "hash64", "hash128", "hash256", "hash512",
-             "hash1024", "hash_block", "window", "merge"]
+             "hash1024", "hash_block", "window", "block_rank", "merge"]
 PHASES = ["h2d", "transpose", "analyze", "symbolic", "scan", "numeric", "d2h", "other"]
 
 # Reference entry points exported with C linkage (include/appt_spgemm.h, layer 1).

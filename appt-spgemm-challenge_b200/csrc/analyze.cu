@@ -140,6 +140,7 @@ __device__ __forceinline__ int num_bin_of(int method, long long nnz, long long f
     if (bytes <= 4608) return kNumRank4K + group_index(flop, rowlen);
     if (bytes <= 9216) return kNumRank8K + group_index(flop, rowlen);
     if (nnz > 512 && span <= kWindowCols && span <= 4 * nnz) return kNumWindow;
+    if (nnz > kHashBlockSlots / 2) return kNumBlockRank;
   }
   if (nnz <= 32) return kNumHash64;
   if (nnz <= 64) return kNumHash128;

@@ -434,7 +434,7 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
                            sms, s);
     else
       launch_numeric(b, rows_num, boff_num, nr, A, B, upper, row_base, lo, hi, flop, handoff, crp,
-                     cci, cval, err, sms, s);
+                     cci, cval, err + 2, err, sms, s);
     note_launches(1);
   }
   tm.end();

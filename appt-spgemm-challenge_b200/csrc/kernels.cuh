@@ -74,7 +74,8 @@ enum NumBin : int {
   kNumHash512,
   kNumHash1024,
   kNumHashBlock,   // CTA per row, 8192-slot table
-  kNumWindow,      // CTA per row, dense windows of 16384 columns (heavy rows)
+  kNumWindow,      // CTA per row, dense windows of 16384 columns (dense heavy rows)
+  kNumBlockRank,   // CTA per row, bitmap rank over 2^20-column windows, sums in C (long rows)
   kNumMerge,       // warp per row, k-way merge of the row's B rows (merge method)
   kNumNumBins
 };
@@ -119,10 +120,11 @@ void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, 
                      int* row_nnz, RowBitmaps handoff, int* err, int num_sms, cudaStream_t s);
 
 // numeric.cu
+// row_counter: a zeroed int (the CTA tiers take rows from it dynamically)
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows_host,
                     Csr A, Csr B, int upper, int row_base, const int* lo, const int* hi,
                     const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
-                    double* cval, int* err, int num_sms, cudaStream_t s);
+                    double* cval, int* row_counter, int* err, int num_sms, cudaStream_t s);
 
 // merge.cu
 void launch_merge_count(const int* rows, const long long* bin_off, int bin, Csr A, Csr B,

@@ -207,7 +207,7 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
     const long long nr = boff[b + 1] - boff[b];
     if (nr <= 0) continue;
     launch_numeric(b, rows_num, boff_num, nr, dA, dB, 0, 0, lo, hi, flop, RowBitmaps{}, crp, cci, cval,
-                   err, sms, s);
+                   err + 2, err, sms, s);
     note_launches(1);
   }
   e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s);

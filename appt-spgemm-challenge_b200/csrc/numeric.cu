@@ -210,6 +210,175 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
   }
 }
 
+// --------------------------------------------------------------------------- CTA rank tier
+// Long rows (more than 4096 entries) whose span is too sparse for dense windows: one CTA per row
+// (rows taken dynamically from a counter), the span cut into windows of 32 * MAXW columns. Per
+// window: presence bitmap in shared memory, a 16-bit popcount prefix per word relative to the
+// owning thread's run of words plus the thread's base, then C's columns are written straight
+// from the bitmap (ranks are output positions) with their sums zeroed, and every product is
+// added into C at its rank with a global fp64 atomic (the row of C stays in L2 while the CTA
+// works on it).
+//
+// Work split: the row's A entries are taken NT at a time; each B row (its part inside the
+// window) is cut into pieces of at most kPiece entries and the warps take pieces round-robin,
+// so a row made of a few very long B rows keeps every warp busy.
+constexpr int kPiece = 256;
+
+struct BlockChunk {   // one chunk of up to NT A entries of a row, in shared memory
+  int* piece_ex;      // exclusive prefix of pieces per entry
+  int* bs;            // B segment start (inside the window)
+  int* be;            // B segment end
+  double* a;          // A value
+};
+
+// Loads A entries [cb, cb + NT) of the row (segments restricted to [w0, w1) when `multi`) and
+// returns the number of pieces. Contains barriers.
+template <int NT>
+__device__ __forceinline__ int load_block_chunk(const Csr& A, const Csr& B, int cb, int re,
+                                                bool multi, long long w0, long long w1,
+                                                BlockChunk ch, long long* sbuf) {
+  const int tid = threadIdx.x;
+  const int p = cb + tid;
+  int bs = 0, be = 0;
+  double a = 0.0;
+  if (p < re) {
+    const int k = __ldg(A.ci + p);
+    bs = __ldg(B.rp + k);
+    be = __ldg(B.rp + k + 1);
+    a = __ldg(A.val + p);
+    if (multi) {
+      bs = lower_bound_col(B.ci, bs, be, (int)w0);
+      be = lower_bound_col(B.ci, bs, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
+    }
+  }
+  const int pieces = (be - bs + kPiece - 1) / kPiece;
+  long long tot;
+  const long long ex = block_excl_scan_ll<NT>(pieces, sbuf, &tot);
+  ch.piece_ex[tid] = (int)ex;
+  ch.bs[tid] = bs;
+  ch.be[tid] = be;
+  ch.a[tid] = a;
+  __syncthreads();
+  return (int)tot;
+}
+
+template <int NT, int MAXW>
+__global__ void __launch_bounds__(NT, 1) num_block_rank_kernel(
+    const int* rows, const long long* bin_off, int bin, Csr A, Csr B, const int* lo_arr,
+    const int* hi_arr, const long long* crp, int* cci, double* cval, int* row_counter, int* err) {
+  extern __shared__ __align__(16) unsigned char num_smem[];
+  constexpr int NW = NT / 32;
+  constexpr long long WCOLS = 32ll * MAXW;
+  unsigned* bm = reinterpret_cast<unsigned*>(num_smem);                   // [MAXW]
+  unsigned short* pre = reinterpret_cast<unsigned short*>(bm + MAXW);     // [MAXW]
+  unsigned* tbase = reinterpret_cast<unsigned*>(pre + MAXW);              // [NT]
+  BlockChunk ch;
+  ch.a = reinterpret_cast<double*>(tbase + NT);                           // [NT]
+  ch.piece_ex = reinterpret_cast<int*>(ch.a + NT);                        // [NT]
+  ch.bs = ch.piece_ex + NT;                                               // [NT]
+  ch.be = ch.bs + NT;                                                     // [NT]
+  __shared__ long long sbuf[NW + 1];
+  __shared__ long long s_row;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long long b0 = bin_off[bin];
+  const long long nrows = bin_off[bin + 1] - b0;
+  for (;;) {
+    if (tid == 0) s_row = atomicAdd(row_counter, 1);
+    __syncthreads();
+    const long long r = s_row;
+    if (r >= nrows) break;
+    const int i = rows[b0 + r];
+    const int lo = lo_arr[i], hi = hi_arr[i];
+    const long long c0 = crp[i];
+    const long long n = crp[i + 1] - c0;
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    const bool multi = (long long)hi - lo + 1 > WCOLS;
+    long long ob = 0;   // entries emitted by the earlier windows of the row
+    for (long long w0 = lo; w0 <= hi; w0 += WCOLS) {
+      const long long w1 = (w0 + WCOLS < (long long)hi + 1) ? w0 + WCOLS : (long long)hi + 1;
+      const unsigned span = (unsigned)(w1 - w0);
+      const int W = (int)((span + 31) >> 5);
+      int lp = 0;
+      while ((NT << lp) < W) ++lp;   // each thread owns 2^lp consecutive words
+      for (int w = tid; w < W; w += NT) bm[w] = 0u;
+      // 1) presence bitmap
+      for (int cb = rs; cb < re; cb += NT) {
+        const int cn = (re - cb) < NT ? (re - cb) : NT;
+        const int tp = load_block_chunk<NT>(A, B, cb, re, multi, w0, w1, ch, sbuf);
+        for (int it = warp; it < tp; it += NW) {
+          const int L = search_le(ch.piece_ex, cn, it);
+          const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
+          const int q1 = (q0 + kPiece < ch.be[L]) ? q0 + kPiece : ch.be[L];
+          for (int q = q0 + lane; q < q1; q += 32) {
+            const unsigned off = (unsigned)((long long)__ldg(B.ci + q) - w0);
+            red_or_shared_if(off < span, bm + (off >> 5), 1u << (off & 31));
+          }
+        }
+        __syncthreads();
+      }
+      // 2) ranks: per-thread runs of 2^lp words, 16-bit prefix within the run + run base
+      const int wa = tid << lp;
+      const int wb = (wa + (1 << lp) < W) ? wa + (1 << lp) : W;
+      int c = 0;
+      for (int w = wa; w < wb; ++w) c += __popc(bm[w]);
+      long long tot;
+      const long long ex = block_excl_scan_ll<NT>(c, sbuf, &tot);
+      tbase[tid] = (unsigned)ex;
+      {
+        int run = 0;
+        for (int w = wa; w < wb; ++w) {
+          pre[w] = (unsigned short)run;
+          run += __popc(bm[w]);
+        }
+      }
+      __syncthreads();
+      if (ob + tot > n) {   // the symbolic count disagrees: report, write nothing more
+        if (tid == 0) set_error(err, kErrCapacity);
+        break;
+      }
+      // 3) columns of C from the bitmap (warp per 32 consecutive words), sums zeroed
+      for (int wq = warp * 32; wq < W; wq += NT) {
+        const int w = wq + lane;
+        unsigned bits = w < W ? bm[w] : 0u;
+        long long rk = w < W ? (long long)tbase[w >> lp] + pre[w] : 0;
+        while (bits) {
+          const int b = __ffs(bits) - 1;
+          bits &= bits - 1;
+          const long long dst = c0 + ob + rk;
+          cci[dst] = (int)(w0 + 32ll * w + b);
+          cval[dst] = 0.0;
+          ++rk;
+        }
+      }
+      __syncthreads();   // the zeroed sums are visible to the whole block before the atomics
+      // 4) every product added at its rank
+      for (int cb = rs; cb < re; cb += NT) {
+        const int cn = (re - cb) < NT ? (re - cb) : NT;
+        const int tp = load_block_chunk<NT>(A, B, cb, re, multi, w0, w1, ch, sbuf);
+        for (int it = warp; it < tp; it += NW) {
+          const int L = search_le(ch.piece_ex, cn, it);
+          const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
+          const int q1 = (q0 + kPiece < ch.be[L]) ? q0 + kPiece : ch.be[L];
+          const double a = ch.a[L];
+          for (int q = q0 + lane; q < q1; q += 32) {
+            const unsigned off = (unsigned)((long long)__ldg(B.ci + q) - w0);
+            if (off < span) {
+              const unsigned w = off >> 5;
+              const long long rk = (long long)tbase[w >> lp] + pre[w] +
+                                   __popc(bm[w] & ((1u << (off & 31)) - 1u));
+              atomicAdd(cval + c0 + ob + rk, __dmul_rn(a, __ldg(B.val + q)));
+            }
+          }
+        }
+        __syncthreads();
+      }
+      ob += tot;
+    }
+    if (tid == 0 && ob != n) set_error(err, kErrCapacity);
+    __syncthreads();
+  }
+}
+
 // --------------------------------------------------------------------------- CTA hash tier
 template <int T, int NT>
 __global__ void __launch_bounds__(NT) num_block_hash_kernel(
@@ -479,7 +648,7 @@ void run_warp_rank(int bin, int gidx, const int* rows, const long long* bin_off,
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
                     Csr B, int upper, int row_base, const int* lo, const int* hi,
                     const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
-                    double* cval, int* err, int num_sms, cudaStream_t s) {
+                    double* cval, int* row_counter, int* err, int num_sms, cudaStream_t s) {
   if (nrows <= 0) return;
   if (bin >= kNumRank2K && bin < kNumRank2K + 3) {
     run_warp_rank<2304, 8>(bin, bin - kNumRank2K, rows, bin_off, nrows, A, B, upper, row_base, lo,
@@ -528,6 +697,20 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
       }
       const int grid = occupancy_grid(kern, NT, smem, num_sms, nrows, 1);
       kern<<<grid, NT, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, crp, cci, cval, err);
+      break;
+    }
+    case kNumBlockRank: {
+      constexpr int NT = 1024, MAXW = 32768;
+      const size_t smem = (size_t)MAXW * 6 + (size_t)NT * (4 + 8 + 12);
+      auto kern = num_block_rank_kernel<NT, MAXW>;
+      static bool attr = false;
+      if (!attr) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = true;
+      }
+      const long long grid = nrows < num_sms ? nrows : num_sms;
+      kern<<<(unsigned)grid, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, crp, cci, cval,
+                                            row_counter, err);
       break;
     }
     case kNumWindow: {

@@ -90,9 +90,62 @@ def test_all_tiers(tier_matrix, method):
     C, st = check(tier_matrix, method=method)
     used = {k for k, v in st["tier_rows"].items() if v > 0}
     if method == "adaptive":
-        assert {"rank2k", "hash64", "hash_block", "window"} <= used, used
+        assert {"rank2k", "hash64", "hash_block", "block_rank"} <= used, used
+    if method == "hash":
+        assert {"hash64", "hash_block", "window"} <= used, used
     if method == "merge":
         assert "merge" in used and "window" in used, used
+
+
+def _hub_matrix(n=1 << 17, hubs=24, hub_len=6000, seed=9):
+    """Sparse rows plus a few hub rows with thousands of entries spread over the whole column
+    range: rows of A*A that reach a hub have more than 4096 entries on a sparse, wide span (the
+    CTA rank tier); the hub rows themselves span up to 2^17 columns."""
+    rng = np.random.default_rng(seed)
+    rows = []
+    hub_ids = rng.choice(n, hubs, replace=False)
+    for i in range(n):
+        L = hub_len if i in hub_ids else int(rng.integers(1, 6))
+        rows.append(np.unique(rng.integers(0, n, L)))
+    rp = np.zeros(n + 1, np.int64)
+    rp[1:] = np.cumsum([len(r) for r in rows])
+    ci = np.concatenate(rows).astype(np.int32)
+    return M.Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))
+
+
+@pytest.mark.parametrize("op", ["ab", "aat_upper"])
+def test_block_rank_tier(op):
+    A = _hub_matrix()
+    C, st = check(A, op=op)
+    assert st["tier_rows"]["block_rank"] > 0, st["tier_rows"]
+
+
+def test_window_tier_dense_rows():
+    """Rows of C with more than ~600 entries packed into at most 16384 columns take the dense
+    window tier."""
+    rng = np.random.default_rng(8)
+    n = 8192
+    rows = [np.unique(np.clip(i + rng.integers(-2000, 2000, 800), 0, n - 1)) for i in range(n)]
+    rp = np.zeros(n + 1, np.int64)
+    rp[1:] = np.cumsum([len(r) for r in rows])
+    ci = np.concatenate(rows).astype(np.int32)
+    A = M.Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))
+    C, st = check(A)
+    assert st["tier_rows"]["window"] > 0, st["tier_rows"]
+
+
+def test_block_rank_multiwindow():
+    """Rows of C spanning more than 2^20 columns are processed in several bitmap windows."""
+    rng = np.random.default_rng(4)
+    k, cols = 64, 1 << 22
+    brows = [np.unique(rng.integers(0, cols, 3000)) for _ in range(k)]
+    brp = np.zeros(k + 1, np.int64)
+    brp[1:] = np.cumsum([len(r) for r in brows])
+    bci = np.concatenate(brows).astype(np.int32)
+    B = M.Csr(k, cols, brp.astype(np.int32), bci, rng.uniform(-1, 1, bci.size))
+    A = M.random_csr(96, k, 0.25, 5)
+    C, st = check(A, B)
+    assert st["tier_rows"]["block_rank"] > 0, st["tier_rows"]
 
 
 @pytest.mark.parametrize("method", ["adaptive", "hash", "esc"])
@@ -103,7 +156,8 @@ def test_sequential_tiers_are_bit_exact(name, method):
     bit (the CTA tiers, used only for rows beyond 512 entries, accumulate with atomics)."""
     A = M.random_csr(2000, 2000, 0.005, 4) if name == "random" else M.make(name, small=True)
     C, st = ap.spgemm(A, method=method, return_stats=True)
-    assert st["bin_rows"]["hash_block"] == 0 and st["bin_rows"]["window"] == 0
+    assert st["tier_rows"]["hash_block"] == 0 and st["tier_rows"]["window"] == 0
+    assert st["tier_rows"]["block_rank"] == 0
     R = oracle.spgemm(A)
     assert_same_structure(C, R)
     assert np.array_equal(C.val, R.val)
