@@ -376,7 +376,7 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   if (m > 0) {
     for (int b = 0; b < kNumSymBins; ++b)
       launch_symbolic(b, rows_sym, boff_sym, A, B, upper, row_base, lo, hi, flop, row_nnz, handoff,
-                      err, sms, s);
+                      err + 3, err, sms, s);
     note_launches(kNumSymBins);
     if (method == kMethodMerge) {
       launch_merge_count(rows_sym, boff_sym, kSymMergeBin, A, B, upper, row_base, row_nnz, err,

@@ -115,9 +115,11 @@ void launch_classify_numeric(Csr A, int m, int method, const long long* flop, co
                              cudaStream_t s);
 
 // symbolic.cu
+// row_counter: a zeroed int (the CTA tier takes rows from it dynamically)
 void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
                      int row_base, const int* lo, const int* hi, const long long* flop,
-                     int* row_nnz, RowBitmaps handoff, int* err, int num_sms, cudaStream_t s);
+                     int* row_nnz, RowBitmaps handoff, int* row_counter, int* err, int num_sms,
+                     cudaStream_t s);
 
 // numeric.cu
 // row_counter: a zeroed int (the CTA tiers take rows from it dynamically)

@@ -219,49 +219,6 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
 // added into C at its rank with a global fp64 atomic (the row of C stays in L2 while the CTA
 // works on it).
 //
-// Work split: the row's A entries are taken NT at a time; each B row (its part inside the
-// window) is cut into pieces of at most kPiece entries and the warps take pieces round-robin,
-// so a row made of a few very long B rows keeps every warp busy.
-constexpr int kPiece = 256;
-
-struct BlockChunk {   // one chunk of up to NT A entries of a row, in shared memory
-  int* piece_ex;      // exclusive prefix of pieces per entry
-  int* bs;            // B segment start (inside the window)
-  int* be;            // B segment end
-  double* a;          // A value
-};
-
-// Loads A entries [cb, cb + NT) of the row (segments restricted to [w0, w1) when `multi`) and
-// returns the number of pieces. Contains barriers.
-template <int NT>
-__device__ __forceinline__ int load_block_chunk(const Csr& A, const Csr& B, int cb, int re,
-                                                bool multi, long long w0, long long w1,
-                                                BlockChunk ch, long long* sbuf) {
-  const int tid = threadIdx.x;
-  const int p = cb + tid;
-  int bs = 0, be = 0;
-  double a = 0.0;
-  if (p < re) {
-    const int k = __ldg(A.ci + p);
-    bs = __ldg(B.rp + k);
-    be = __ldg(B.rp + k + 1);
-    a = __ldg(A.val + p);
-    if (multi) {
-      bs = lower_bound_col(B.ci, bs, be, (int)w0);
-      be = lower_bound_col(B.ci, bs, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
-    }
-  }
-  const int pieces = (be - bs + kPiece - 1) / kPiece;
-  long long tot;
-  const long long ex = block_excl_scan_ll<NT>(pieces, sbuf, &tot);
-  ch.piece_ex[tid] = (int)ex;
-  ch.bs[tid] = bs;
-  ch.be[tid] = be;
-  ch.a[tid] = a;
-  __syncthreads();
-  return (int)tot;
-}
-
 template <int NT, int MAXW>
 __global__ void __launch_bounds__(NT, 1) num_block_rank_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, const int* lo_arr,

@@ -225,103 +225,68 @@ void launch_sym_bitmap(int bin, int gidx, const int* rows, const long long* bin_
                                        row_nnz, handoff, err, num_sms, s);
 }
 
-// CTA per row. Bitmap windows of WB words (32*WB columns) over [lo, hi]; rows whose span exceeds
-// one window restrict every B row to the window by binary search (B rows are sorted).
+// CTA per row (rows taken dynamically from a counter). Bitmap windows of WB words (32 * WB
+// columns) over [lo, hi]; rows whose span exceeds one window restrict every B row to the window
+// by binary search (B rows are sorted). The warps share the products in pieces
+// (load_block_chunk, walk.cuh), set bits with fire-and-forget shared OR operations, and the
+// window's columns are counted by popcount.
 template <int NT, int WB>
-__global__ void __launch_bounds__(NT) sym_block_kernel(const int* rows, const long long* bin_off,
-                                                       int bin, Csr A, Csr B, int upper,
-                                                       int row_base, const int* lo_arr,
-                                                       const int* hi_arr, int* row_nnz, int* err) {
-  extern __shared__ unsigned sym_smem[];
-  unsigned* bm = sym_smem;                                   // [WB]
-  long long* excl_s = (long long*)(sym_smem + WB);           // [NT + 1]
-  int* bs_s = (int*)(excl_s + NT + 1);                       // [NT]
-  __shared__ long long wsum[NT / 32 + 1];
-  __shared__ int red[NT / 32];
+__global__ void __launch_bounds__(NT, 1) sym_block_kernel(const int* rows, const long long* bin_off,
+                                                          int bin, Csr A, Csr B, const int* lo_arr,
+                                                          const int* hi_arr, int* row_nnz,
+                                                          int* row_counter) {
+  extern __shared__ __align__(16) unsigned char sym_block_smem[];
+  constexpr int NW = NT / 32;
+  constexpr long long WCOLS = 32ll * WB;
+  unsigned* bm = reinterpret_cast<unsigned*>(sym_block_smem);   // [WB]
+  BlockChunk ch;
+  ch.a = reinterpret_cast<double*>(bm + WB);                     // [NT] (unused here)
+  ch.piece_ex = reinterpret_cast<int*>(ch.a + NT);               // [NT]
+  ch.bs = ch.piece_ex + NT;                                      // [NT]
+  ch.be = ch.bs + NT;                                            // [NT]
+  __shared__ long long sbuf[NW + 1];
+  __shared__ long long s_row;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
-  for (long long r = blockIdx.x; r < nrows; r += gridDim.x) {
+  for (;;) {
+    if (tid == 0) s_row = atomicAdd(row_counter, 1);
+    __syncthreads();
+    const long long r = s_row;
+    if (r >= nrows) break;
     const int i = rows[b0 + r];
-    const int ig = i + row_base;
     const int lo = lo_arr[i], hi = hi_arr[i];
     const int rs = A.rp[i], re = A.rp[i + 1];
-    const long long span = (long long)hi - lo + 1;
-    const bool multi = span > 32ll * WB;
-    int cnt = 0;
-    for (long long w0 = lo; w0 <= hi; w0 += 32ll * WB) {
-      const long long w1 = (w0 + 32ll * WB < (long long)hi + 1) ? w0 + 32ll * WB : (long long)hi + 1;
-      const int nwords = (int)((w1 - w0 + 31) >> 5);
-      for (int w = tid; w < nwords; w += NT) bm[w] = 0u;
-      __syncthreads();
-      for (int base = rs; base < re; base += NT) {
-        const int p = base + tid;
-        int bs = 0, be = 0;
-        if (p < re) {
-          const int k = A.ci[p];
-          bs = B.rp[k];
-          be = B.rp[k + 1];
-          if (multi) {
-            const int s2 = lower_bound_col(B.ci, bs, be, (int)w0);
-            be = lower_bound_col(B.ci, s2, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
-            bs = s2;
+    const bool multi = (long long)hi - lo + 1 > WCOLS;
+    long long cnt = 0;
+    for (long long w0 = lo; w0 <= hi; w0 += WCOLS) {
+      const long long w1 = (w0 + WCOLS < (long long)hi + 1) ? w0 + WCOLS : (long long)hi + 1;
+      const unsigned span = (unsigned)(w1 - w0);
+      const int W = (int)((span + 31) >> 5);
+      for (int w = tid; w < W; w += NT) bm[w] = 0u;
+      for (int cb = rs; cb < re; cb += NT) {
+        const int cn = (re - cb) < NT ? (re - cb) : NT;
+        const int tp = load_block_chunk<NT>(A, B, cb, re, multi, w0, w1, ch, sbuf);
+        for (int it = warp; it < tp; it += NW) {
+          const int L = search_le(ch.piece_ex, cn, it);
+          const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
+          const int q1 = (q0 + kPiece < ch.be[L]) ? q0 + kPiece : ch.be[L];
+          for (int q = q0 + lane; q < q1; q += 32) {
+            const unsigned off = (unsigned)((long long)__ldg(B.ci + q) - w0);
+            red_or_shared_if(off < span, bm + (off >> 5), 1u << (off & 31));
           }
-        }
-        // block exclusive scan of segment lengths (int64)
-        long long len = be - bs;
-        long long incl = len;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          long long y = __shfl_up_sync(kFull, incl, o);
-          if (lane >= o) incl += y;
-        }
-        if (lane == 31) wsum[warp] = incl;
-        __syncthreads();
-        if (warp == 0) {
-          long long x = lane < NT / 32 ? wsum[lane] : 0;
-          long long xi = x;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            long long y = __shfl_up_sync(kFull, xi, o);
-            if (lane >= o) xi += y;
-          }
-          if (lane < NT / 32) wsum[lane] = xi - x;
-          if (lane == NT / 32 - 1) wsum[NT / 32] = xi;
-        }
-        __syncthreads();
-        excl_s[tid] = wsum[warp] + incl - len;
-        bs_s[tid] = bs;
-        const long long total = wsum[NT / 32];
-        __syncthreads();
-        for (long long t = tid; t < total; t += NT) {
-          // owner: largest L with excl_s[L] <= t
-          int lo_i = 0, hi_i = NT - 1;
-          while (lo_i < hi_i) {
-            int mid = (lo_i + hi_i + 1) >> 1;
-            if (excl_s[mid] <= t) lo_i = mid; else hi_i = mid - 1;
-          }
-          const int j = B.ci[bs_s[lo_i] + (int)(t - excl_s[lo_i])];
-          if (upper && j < ig) continue;
-          if (j < w0 || j >= w1) continue;
-          const unsigned off = (unsigned)(j - w0);
-          const unsigned bit = 1u << (off & 31);
-          const unsigned old = atomicOr(&bm[off >> 5], bit);
-          cnt += (old & bit) ? 0 : 1;
         }
         __syncthreads();
       }
+      int c = 0;
+      for (int w = tid; w < W; w += NT) c += __popc(bm[w]);
+      long long tot;
+      block_excl_scan_ll<NT>(c, sbuf, &tot);
+      cnt += tot;
     }
-    cnt = warp_sum(cnt);
-    if (lane == 0) red[warp] = cnt;
-    __syncthreads();
-    if (tid == 0) {
-      int s = 0;
-      for (int w = 0; w < NT / 32; ++w) s += red[w];
-      row_nnz[i] = s;
-    }
+    if (tid == 0) row_nnz[i] = (int)(cnt < 0x7fffffffll ? cnt : 0x7fffffffll);
     __syncthreads();
   }
-  (void)err;
 }
 
 template <int WORDS, int WPB>
@@ -346,7 +311,8 @@ void launch_sym_warp(int bin, const int* rows, const long long* bin_off, Csr A, 
 
 void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
                      int row_base, const int* lo, const int* hi, const long long* flop,
-                     int* row_nnz, RowBitmaps handoff, int* err, int num_sms, cudaStream_t s) {
+                     int* row_nnz, RowBitmaps handoff, int* row_counter, int* err, int num_sms,
+                     cudaStream_t s) {
   if (bin >= kSymBmS && bin < kSymBmM) {
     launch_sym_bitmap<256, 8>(bin, bin - kSymBmS, rows, bin_off, A, B, upper, row_base, lo, hi,
                               flop, row_nnz, handoff, err, num_sms, s);
@@ -376,16 +342,15 @@ void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, 
                                err, num_sms, s);
       break;
     case kSymBlock: {
-      constexpr int NT = 512;
-      const size_t smem = (size_t)kSymBlockWords * 4 + (NT + 1) * 8 + NT * 4;
+      constexpr int NT = 1024;
+      const size_t smem = (size_t)kSymBlockWords * 4 + (size_t)NT * (8 + 12);
       auto kern = sym_block_kernel<NT, kSymBlockWords>;
       static bool attr_set = false;
       if (!attr_set) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr_set = true;
       }
-      kern<<<num_sms, NT, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, row_nnz,
-                                     err);
+      kern<<<num_sms, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, row_nnz, row_counter);
       break;
     }
     default:
