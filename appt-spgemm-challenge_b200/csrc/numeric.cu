@@ -266,9 +266,12 @@ __global__ void __launch_bounds__(NT, 1) num_block_rank_kernel(
           const int L = search_le(ch.piece_ex, cn, it);
           const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
           const int q1 = (q0 + kPiece < ch.be[L]) ? q0 + kPiece : ch.be[L];
-          for (int q = q0 + lane; q < q1; q += 32) {
-            const unsigned off = (unsigned)((long long)__ldg(B.ci + q) - w0);
-            red_or_shared_if(off < span, bm + (off >> 5), 1u << (off & 31));
+          for (int q = q0 + lane; q < q1; q += 128) {
+            PieceRound pr;
+            load_piece_round<false>(B, q, q1, w0, pr);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              red_or_shared_if(pr.off[u] < span, bm + (pr.off[u] >> 5), 1u << (pr.off[u] & 31));
           }
         }
         __syncthreads();
@@ -317,13 +320,18 @@ __global__ void __launch_bounds__(NT, 1) num_block_rank_kernel(
           const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
           const int q1 = (q0 + kPiece < ch.be[L]) ? q0 + kPiece : ch.be[L];
           const double a = ch.a[L];
-          for (int q = q0 + lane; q < q1; q += 32) {
-            const unsigned off = (unsigned)((long long)__ldg(B.ci + q) - w0);
-            if (off < span) {
-              const unsigned w = off >> 5;
-              const long long rk = (long long)tbase[w >> lp] + pre[w] +
-                                   __popc(bm[w] & ((1u << (off & 31)) - 1u));
-              atomicAdd(cval + c0 + ob + rk, __dmul_rn(a, __ldg(B.val + q)));
+          for (int q = q0 + lane; q < q1; q += 128) {
+            PieceRound pr;
+            load_piece_round<true>(B, q, q1, w0, pr);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const unsigned off = pr.off[u];
+              if (off < span) {
+                const unsigned w = off >> 5;
+                const long long rk = (long long)tbase[w >> lp] + pre[w] +
+                                     __popc(bm[w] & ((1u << (off & 31)) - 1u));
+                atomicAdd(cval + c0 + ob + rk, __dmul_rn(a, pr.x[u]));
+              }
             }
           }
         }

@@ -271,9 +271,12 @@ __global__ void __launch_bounds__(NT, 1) sym_block_kernel(const int* rows, const
           const int L = search_le(ch.piece_ex, cn, it);
           const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
           const int q1 = (q0 + kPiece < ch.be[L]) ? q0 + kPiece : ch.be[L];
-          for (int q = q0 + lane; q < q1; q += 32) {
-            const unsigned off = (unsigned)((long long)__ldg(B.ci + q) - w0);
-            red_or_shared_if(off < span, bm + (off >> 5), 1u << (off & 31));
+          for (int q = q0 + lane; q < q1; q += 128) {
+            PieceRound pr;
+            load_piece_round<false>(B, q, q1, w0, pr);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              red_or_shared_if(pr.off[u] < span, bm + (pr.off[u] >> 5), 1u << (pr.off[u] & 31));
           }
         }
         __syncthreads();

@@ -242,28 +242,34 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
   constexpr int L = 32 / G;
   const int lane = threadIdx.x & 31, grp = lane / L, sub = lane % L;
   if (!__any_sync(kFull, len > L)) {
+    // software pipeline: entries loaded two steps ahead, their rank looked up one step ahead
+    // (the bitmap is read-only here), so a step's critical path is the accumulator update alone
     double x0, x1;
-    int j0 = load_b_entry(B, __shfl_sync(kFull, bs, grp), __shfl_sync(kFull, len, grp), sub, lo,
-                          &x0);
+    const int j0 = load_b_entry(B, __shfl_sync(kFull, bs, grp), __shfl_sync(kFull, len, grp),
+                                sub, lo, &x0);
     int j1 = load_b_entry(B, __shfl_sync(kFull, bs, G + grp), __shfl_sync(kFull, len, G + grp),
                           sub, lo, &x1);
+    unsigned off0 = (unsigned)(j0 - lo);
+    int r0 = rank_or(bm, pre, off0, span, n);
     for (int t0 = 0; t0 < cnt; t0 += G) {
       // entries two steps ahead (a step past the chunk reads a valid row and is discarded)
       const int t2 = (t0 + 2 * G + grp) & 31;
       double x2;
       const int j2 = load_b_entry(B, __shfl_sync(kFull, bs, t2), __shfl_sync(kFull, len, t2),
                                   sub, lo, &x2);
+      const unsigned off1 = (unsigned)(j1 - lo);
+      const int r1 = rank_or(bm, pre, off1, span, n);
       const double at = __shfl_sync(kFull, a, t0 + grp);
-      const unsigned off = (unsigned)(j0 - lo);
-      const int r = rank_or(bm, pre, off, span, n);
+      const double p0 = __dmul_rn(at, x0);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const int pos = (G == 1 || grp == g) ? r : n;
-        acc[pos] = mul_add_rn(acc[pos], at, x0);
-        coff[pos] = (unsigned short)off;
+        const int pos = (G == 1 || grp == g) ? r0 : n;
+        acc[pos] = __dadd_rn(acc[pos], p0);
+        coff[pos] = (unsigned short)off0;
         __syncwarp();
       }
-      j0 = j1;
+      off0 = off1;
+      r0 = r1;
       x0 = x1;
       j1 = j2;
       x1 = x2;
@@ -334,6 +340,28 @@ __device__ __forceinline__ int load_block_chunk(const Csr& A, const Csr& B, int 
   ch.a[tid] = a;
   __syncthreads();
   return (int)tot;
+}
+
+// Entries [q0, q1) of a B row, four rounds of 32 per lane-step with all loads issued before any
+// is used: columns (as offsets from the window start w0; entries past q1 get an offset outside
+// every window) and, when `x` is given, values.
+struct PieceRound {
+  unsigned off[4];
+  double x[4];
+};
+
+template <bool WITH_VAL>
+__device__ __forceinline__ void load_piece_round(const Csr& B, int q, int q1, long long w0,
+                                                 PieceRound& pr) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int qq = q + 32 * u;
+    const bool v = qq < q1;
+    const int idx = v ? qq : q;   // q < q1: always a valid entry
+    const int j = __ldg(B.ci + idx);
+    if (WITH_VAL) pr.x[u] = __ldg(B.val + idx);
+    pr.off[u] = v ? (unsigned)((long long)j - w0) : 0xffffffffu;
+  }
 }
 
 }  // namespace appt
