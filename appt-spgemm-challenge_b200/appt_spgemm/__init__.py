@@ -216,9 +216,44 @@ def _take_host_out(out: CsrOut) -> Csr:
     return Csr(rows, int(out.cols), rp, ci, va)
 
 
+class _HostOut:
+    """Owner of a host result block (released to the library when the last view goes away)."""
+
+    def __init__(self, out: CsrOut):
+        self.out = out
+
+    def __del__(self):
+        try:
+            load().appt_free_out(ct.byref(self.out))
+        except Exception:
+            pass
+
+
+def _view_host_out(out: CsrOut) -> Csr:
+    """Csr whose arrays are views of the library's (pinned) result block; the block is released
+    when the Csr is (keep the Csr, not only its arrays)."""
+    owner = _HostOut(out)
+    rows, nnz = int(out.rows), int(out.nnz)
+
+    def view(ptr, ctype, n, dtype):
+        if n == 0:
+            return np.zeros(0, dtype)
+        return np.frombuffer((ctype * n).from_address(ptr), dtype=dtype)
+
+    rp = np.frombuffer((ct.c_int64 * (rows + 1)).from_address(out.row_ptr), dtype=np.int64)
+    ci = view(out.col_idx, ct.c_int32, nnz, np.int32)
+    va = view(out.val, ct.c_double, nnz, np.float64)
+    C = Csr(rows, int(out.cols), rp, ci, va)
+    C._owner = owner
+    return C
+
+
 def spgemm(A: Csr, B: Csr | None = None, op: str = "ab", method: str = "adaptive",
-           device: int = 0, timing: bool = False, return_stats: bool = False):
-    """C = op(A, B) with host operands; returns a Csr with int64 row_ptr (and stats)."""
+           device: int = 0, timing: bool = False, return_stats: bool = False,
+           copy: bool = True):
+    """C = op(A, B) with host operands; returns a Csr with int64 row_ptr (and stats). With
+    copy=False the arrays are views of the library's pinned result block (no host copy), valid
+    while the returned Csr is alive."""
     lib = load()
     keep: list = []
     a = _host_in(A, keep)
@@ -229,6 +264,9 @@ def spgemm(A: Csr, B: Csr | None = None, op: str = "ab", method: str = "adaptive
     rc = lib.appt_spgemm(ct.byref(a), ct.byref(b) if b is not None else None, ct.byref(o),
                          ct.byref(out), ct.byref(st))
     _check(rc, "appt_spgemm")
+    if not copy:
+        C = _view_host_out(out)
+        return (C, st.as_dict()) if return_stats else C
     try:
         C = _take_host_out(out)
     finally:

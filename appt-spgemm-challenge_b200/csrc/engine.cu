@@ -601,6 +601,58 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
                          opt.method, s, sc, tm, dc, st);
 }
 
+// Pinned host blocks for results returned in host memory: a block released by free_out is kept
+// for the next result that fits (pinning hundreds of MB costs far more than the copy into it);
+// at most kPinnedCacheBytes stay cached.
+static std::mutex g_pin_mu;
+static std::vector<std::pair<void*, size_t>> g_pin_free;
+static size_t g_pin_cached = 0;
+static constexpr size_t kPinnedCacheBytes = size_t(16) << 30;
+static std::vector<std::pair<void*, size_t>> g_pin_live;
+
+static void* pinned_take(size_t bytes) {
+  {
+    std::lock_guard<std::mutex> g(g_pin_mu);
+    int best = -1;
+    for (size_t k = 0; k < g_pin_free.size(); ++k)
+      if (g_pin_free[k].second >= bytes &&
+          (best < 0 || g_pin_free[k].second < g_pin_free[(size_t)best].second))
+        best = (int)k;
+    if (best >= 0) {
+      auto blk = g_pin_free[(size_t)best];
+      g_pin_free.erase(g_pin_free.begin() + best);
+      g_pin_cached -= blk.second;
+      g_pin_live.push_back(blk);
+      return blk.first;
+    }
+  }
+  void* h = nullptr;
+  if (cudaMallocHost(&h, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> g(g_pin_mu);
+  g_pin_live.push_back({h, bytes});
+  return h;
+}
+
+static void pinned_give_back(void* h) {
+  std::lock_guard<std::mutex> g(g_pin_mu);
+  size_t bytes = 0;
+  for (size_t k = 0; k < g_pin_live.size(); ++k)
+    if (g_pin_live[k].first == h) {
+      bytes = g_pin_live[k].second;
+      g_pin_live.erase(g_pin_live.begin() + (long)k);
+      break;
+    }
+  if (bytes == 0 || g_pin_cached + bytes > kPinnedCacheBytes) {
+    cudaFreeHost(h);
+    return;
+  }
+  g_pin_free.push_back({h, bytes});
+  g_pin_cached += bytes;
+}
+
 int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C,
            CallStats* st) {
   if (!C) {
@@ -633,10 +685,9 @@ int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C
       tm.begin(kPhD2H);
       const size_t bytes = sizeof(long long) * ((size_t)dc.rows + 1) + sizeof(int) * (size_t)dc.nnz +
                            sizeof(double) * (size_t)dc.nnz + 64;
-      void* h = nullptr;
       int kind = 2;
-      if (cudaMallocHost(&h, bytes) != cudaSuccess) {
-        cudaGetLastError();
+      void* h = pinned_take(bytes);
+      if (!h) {
         h = std::malloc(bytes);
         kind = 3;
       }
@@ -709,7 +760,7 @@ int free_out(MatOut* C) {
       cudaFreeAsync(C->val, (cudaStream_t)C->base);
       break;
     case 2:
-      cudaFreeHost(C->base);
+      pinned_give_back(C->base);
       break;
     case 3:
       std::free(C->base);
