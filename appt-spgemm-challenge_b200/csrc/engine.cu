@@ -10,6 +10,7 @@
 //   * every failure returns a status instead of exiting the process.
 #include <cuda_runtime.h>
 #include <algorithm>
+#include <functional>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -61,6 +62,7 @@ struct DeviceCtx {
   int device = -1;
   int num_sms = 0;
   cudaStream_t stream = nullptr;
+  cudaStream_t copy_stream = nullptr;   // device-to-host copies that overlap the numeric phase
   cudaMemPool_t pool = nullptr;
   char* stage = nullptr;   // pinned host staging for small device->host reads
   // bitmap handoff arena (symbolic -> numeric rank tier), allocated on first use and kept: calls
@@ -94,6 +96,7 @@ static int get_ctx(int device, DeviceCtx** out) {
     CK(cudaSetDevice(device));
     CK(cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, device));
     CK(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&c.copy_stream, cudaStreamNonBlocking));
     cudaMemPoolProps props;
     std::memset(&props, 0, sizeof(props));
     props.allocType = cudaMemAllocationTypePinned;
@@ -210,6 +213,24 @@ static const char* kPhaseNames[8] = {"h2d", "transpose", "analyze", "symbolic",
                                      "scan", "numeric",   "d2h",     "other"};
 
 // ------------------------------------------------------------------ device pipeline
+constexpr int kSinkBlocks = 4;   // row blocks of the numeric phase when C goes to the host
+
+// Host destination of C. With a sink, the numeric phase runs in row blocks and the copies of a
+// finished block go out on the copy stream while the next block computes; `alloc` is called
+// once nnz(C) is known and returns the host arrays (exactly one of rp32 / rp64 set).
+struct HostDst {
+  int* rp32 = nullptr;
+  long long* rp64 = nullptr;
+  int* ci = nullptr;
+  double* val = nullptr;
+};
+struct HostSink {
+  std::function<bool(long long nnz, HostDst* d)> alloc;
+  bool done = false;   // the pipeline filled the destination
+  long long nnz = 0;
+  long long cols = 0;
+};
+
 struct DevC {            // device-resident result, allocations owned by the pool
   long long rows = 0, cols = 0, nnz = 0;
   long long* rp = nullptr;
@@ -315,7 +336,7 @@ static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, 
 
 static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
                            int method, cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C,
-                           CallStats* st) {
+                           CallStats* st, HostSink* sink) {
   if (method == kMethodEsc)
     return esc_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st);
   const int m = A.rows;
@@ -390,9 +411,29 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   launch_classify_numeric(A, m, method, flop, lo, hi, row_nnz, numkey, sms, s);
   partition_rows(numkey, m, kNumNumBins, rows_num, boff_num, pscr, s);
   note_launches(m > 0 ? 10 : 0);
+  // with a host sink the numeric phase runs in K row blocks (rows [k*m/K, (k+1)*m/K)), each
+  // bin's share of a block located by binary search in its ascending row list
+  const int K = (sink && m >= 4096) ? kSinkBlocks : 1;
+  long long* bsub = nullptr;
+  int* bctr = nullptr;
+  if (K > 1) {
+    bsub = sc.get<long long>((size_t)kNumNumBins * (K + 1));
+    bctr = sc.get<int>((size_t)K);
+    if (sc.failed) {
+      set_error("device pool allocation failed");
+      return kErrOom;
+    }
+    CK(cudaMemsetAsync(bctr, 0, sizeof(int) * K, s));
+    block_bin_bounds(rows_num, boff_num, kNumNumBins, m, K, bsub, s);
+    note_launches(1);
+  }
 
-  // the one mid-pipeline synchronisation: C's size and the numeric bin sizes
+  // the one mid-pipeline synchronisation: C's size, the numeric bin sizes (and the blocks' first
+  // entries in C)
   char* stg = ctx->stage;
+  for (int k = 1; k < K; ++k)
+    CK(cudaMemcpyAsync(stg + 1024 + 8 * k, crp + (long long)k * m / K, 8, cudaMemcpyDeviceToHost,
+                       s));
   CK(cudaMemcpyAsync(stg, crp + m, 8, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(stg + 8, boff_num, 8 * (kNumNumBins + 1), cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(stg + 256, gst, sizeof(AnalyzeStats), cudaMemcpyDeviceToHost, s));
@@ -418,26 +459,82 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
     st->products = (long long)hst.total_flop;
     for (int b = 0; b < kNumNumBins && b < 32; ++b) st->bin_rows[b] = boff[b + 1] - boff[b];
   }
+  long long cstart[kSinkBlocks + 1];
+  cstart[0] = 0;
+  for (int k = 1; k < K; ++k) std::memcpy(&cstart[k], stg + 1024 + 8 * k, 8);
+  cstart[K] = nnz;
   int* cci = sc.get<int>(nnz);
   double* cval = sc.get<double>(nnz);
   if (sc.failed) {
     set_error("device pool allocation failed for C (" + std::to_string(nnz) + " entries)");
     return kErrOom;
   }
+  HostDst hd;
+  cudaStream_t cs = ctx->copy_stream;
+  cudaEvent_t evs[kSinkBlocks + 1];
+  if (sink) {
+    if (!sink->alloc(nnz, &hd)) {
+      set_error("host allocation failed for C");
+      return kErrOom;
+    }
+    for (int k = 0; k <= K; ++k) CK(cudaEventCreateWithFlags(&evs[k], cudaEventDisableTiming));
+    // row pointers first (converted to int32 for the reference layout)
+    if (hd.rp32) {
+      int* rp32 = sc.get<int>((size_t)m + 1);
+      if (!rp32) {
+        set_error("device pool allocation failed");
+        return kErrOom;
+      }
+      narrow_rowptr(crp, rp32, (long long)m + 1, s);
+      note_launches(1);
+      CK(cudaEventRecord(evs[K], s));
+      CK(cudaStreamWaitEvent(cs, evs[K], 0));
+      CK(cudaMemcpyAsync(hd.rp32, rp32, sizeof(int) * ((size_t)m + 1), cudaMemcpyDeviceToHost,
+                         cs));
+    } else {
+      CK(cudaEventRecord(evs[K], s));
+      CK(cudaStreamWaitEvent(cs, evs[K], 0));
+      CK(cudaMemcpyAsync(hd.rp64, crp, sizeof(long long) * ((size_t)m + 1),
+                         cudaMemcpyDeviceToHost, cs));
+    }
+  }
 
   tm.begin(kPhNumeric);
-  for (int b = 0; b < kNumNumBins; ++b) {
-    const long long nr = boff[b + 1] - boff[b];
-    if (nr <= 0) continue;
-    if (b == kNumMerge)
-      launch_merge_numeric(rows_num, boff_num, b, nr, A, B, upper, row_base, crp, cci, cval, err,
-                           sms, s);
-    else
-      launch_numeric(b, rows_num, boff_num, nr, A, B, upper, row_base, lo, hi, flop, handoff, crp,
-                     cci, cval, err + 2, err, sms, s);
-    note_launches(1);
+  for (int k = 0; k < K; ++k) {
+    for (int b = 0; b < kNumNumBins; ++b) {
+      const long long nr_all = boff[b + 1] - boff[b];
+      if (nr_all <= 0) continue;
+      // bin offsets of this block: bo[b], bo[b + 1] are the block's share of bin b
+      const long long* bo = K > 1 ? bsub + (size_t)b * K + k : boff_num;
+      const long long nr = K > 1 ? nr_all / K + 1 : nr_all;   // grid sizing only
+      int* ctr = K > 1 ? bctr + k : err + 2;
+      if (b == kNumMerge)
+        launch_merge_numeric(rows_num, bo, b, nr, A, B, upper, row_base, crp, cci, cval, err, sms,
+                             s);
+      else
+        launch_numeric(b, rows_num, bo, nr, A, B, upper, row_base, lo, hi, flop, handoff, crp,
+                       cci, cval, ctr, err, sms, s);
+      note_launches(1);
+    }
+    if (sink) {
+      const long long e0 = cstart[k], e1 = cstart[k + 1];
+      CK(cudaEventRecord(evs[k], s));
+      CK(cudaStreamWaitEvent(cs, evs[k], 0));
+      if (e1 > e0) {
+        CK(cudaMemcpyAsync(hd.ci + e0, cci + e0, sizeof(int) * (size_t)(e1 - e0),
+                           cudaMemcpyDeviceToHost, cs));
+        CK(cudaMemcpyAsync(hd.val + e0, cval + e0, sizeof(double) * (size_t)(e1 - e0),
+                           cudaMemcpyDeviceToHost, cs));
+      }
+    }
   }
   tm.end();
+  if (sink) {
+    CK(cudaStreamSynchronize(cs));
+    for (int k = 0; k <= K; ++k) cudaEventDestroy(evs[k]);
+    sink->done = true;
+    sink->nnz = nnz;
+  }
   CK(cudaMemcpyAsync(stg + 512, err, sizeof(int), cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
   std::memcpy(&herr, stg + 512, sizeof(int));
@@ -548,7 +645,8 @@ static void print_prof(const char* tag, const CallStats& st) {
 
 // Core call. Returns C in device memory (pool allocations) in *dc.
 static int run(const MatView& A, const MatView* B, const CallOptions& opt, DeviceCtx* ctx,
-               cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* dc, CallStats* st) {
+               cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* dc, CallStats* st,
+               HostSink* sink) {
   int rc = check_view(A, opt.in_mem, "A");
   if (rc) return rc;
   const bool ab = opt.op == kOpAB || opt.op == kOpABUpper;
@@ -598,7 +696,7 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
   }
   const int upper = (opt.op == kOpAATUpper || opt.op == kOpABUpper) ? 1 : 0;
   return multiply_device(ctx, dA, dB, A.nnz, upper, (int)opt.row_base,
-                         opt.method, s, sc, tm, dc, st);
+                         opt.method, s, sc, tm, dc, st, sink);
 }
 
 // Pinned host blocks for results returned in host memory: a block released by free_out is kept
@@ -653,13 +751,10 @@ static void pinned_give_back(void* h) {
   g_pin_cached += bytes;
 }
 
-int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C,
-           CallStats* st) {
-  if (!C) {
-    set_error("null output");
-    return kErrInvalid;
-  }
-  std::memset((void*)C, 0, sizeof(*C));
+// C = op(A, B) into a host destination chosen by `sink` once nnz(C) is known. The adaptive
+// pipelines fill it block by block while computing; the ESC pipeline copies at the end.
+static int spgemm_to_host(const MatView& A, const MatView* B, const CallOptions& opt,
+                          HostSink* sink, CallStats* st) {
   if (opt.op < 0 || opt.op > 3 || opt.method < 0 || opt.method > 3) {
     set_error("bad op or method");
     return kErrInvalid;
@@ -679,47 +774,137 @@ int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C
   DevC dc;
   {
     Scratch sc(ctx, s);
-    rc = run(A, B, opt, ctx, s, sc, tm, &dc, stp);
-    if (rc == kOk && opt.out_mem == 0) {
-      // host result: pinned allocation owned by the caller (appt_free_out)
+    rc = run(A, B, opt, ctx, s, sc, tm, &dc, stp, sink);
+    if (rc == kOk && !sink->done) {
       tm.begin(kPhD2H);
-      const size_t bytes = sizeof(long long) * ((size_t)dc.rows + 1) + sizeof(int) * (size_t)dc.nnz +
-                           sizeof(double) * (size_t)dc.nnz + 64;
-      int kind = 2;
-      void* h = pinned_take(bytes);
-      if (!h) {
-        h = std::malloc(bytes);
-        kind = 3;
-      }
-      if (!h) {
+      HostDst d;
+      if (!sink->alloc(dc.nnz, &d)) {
         set_error("host allocation failed for C");
         rc = kErrOom;
       } else {
-        char* p = (char*)h;
-        C->rp = (long long*)p;
-        p += sizeof(long long) * ((size_t)dc.rows + 1);
-        C->val = (double*)(((uintptr_t)p + sizeof(int) * (size_t)dc.nnz + 7) & ~(uintptr_t)7);
-        C->ci = (int*)p;
-        cudaMemcpyAsync(C->rp, dc.rp, sizeof(long long) * ((size_t)dc.rows + 1),
-                        cudaMemcpyDeviceToHost, s);
+        if (d.rp32) {
+          int* rp32 = sc.get<int>((size_t)dc.rows + 1);
+          if (rp32) {
+            narrow_rowptr(dc.rp, rp32, dc.rows + 1, s);
+            note_launches(1);
+            cudaMemcpyAsync(d.rp32, rp32, sizeof(int) * ((size_t)dc.rows + 1),
+                            cudaMemcpyDeviceToHost, s);
+          } else {
+            rc = kErrOom;
+          }
+        } else {
+          cudaMemcpyAsync(d.rp64, dc.rp, sizeof(long long) * ((size_t)dc.rows + 1),
+                          cudaMemcpyDeviceToHost, s);
+        }
         if (dc.nnz > 0) {
-          cudaMemcpyAsync(C->ci, dc.ci, sizeof(int) * (size_t)dc.nnz, cudaMemcpyDeviceToHost, s);
-          cudaMemcpyAsync(C->val, dc.val, sizeof(double) * (size_t)dc.nnz, cudaMemcpyDeviceToHost, s);
+          cudaMemcpyAsync(d.ci, dc.ci, sizeof(int) * (size_t)dc.nnz, cudaMemcpyDeviceToHost, s);
+          cudaMemcpyAsync(d.val, dc.val, sizeof(double) * (size_t)dc.nnz, cudaMemcpyDeviceToHost,
+                          s);
         }
-        tm.end();
-        cudaError_t e = cudaStreamSynchronize(s);
-        if (e != cudaSuccess) {
-          set_error(std::string("D2H of C: ") + cudaGetErrorString(e));
-          rc = kErrCuda;
-        }
-        C->mem = 0;
-        C->alloc_kind = kind;
-        C->base = h;
+        sink->done = true;
+        sink->nnz = dc.nnz;
       }
+    }
+    tm.end();
+    if (dc.rp) {
       cudaFreeAsync(dc.rp, s);
       cudaFreeAsync(dc.ci, s);
       cudaFreeAsync(dc.val, s);
-    } else if (rc == kOk) {
+    }
+    const cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess && rc == kOk) {
+      set_error(std::string("D2H of C: ") + cudaGetErrorString(e));
+      rc = kErrCuda;
+    }
+  }
+  tm.finish(stp);
+  stp->launches = kernel_launches() - launches0;
+  sink->cols = dc.cols;
+  if (rc == kOk) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      set_error(std::string("launch error: ") + cudaGetErrorString(e));
+      rc = kErrCuda;
+    }
+  }
+  if (prof_env() && rc == kOk) print_prof("appt-prof", *stp);
+  return rc;
+}
+
+int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C,
+           CallStats* st) {
+  if (!C) {
+    set_error("null output");
+    return kErrInvalid;
+  }
+  std::memset((void*)C, 0, sizeof(*C));
+  if (opt.out_mem == 0) {
+    // host result: one pinned block [int64 row_ptr | col_idx | val] owned by the caller
+    // (appt_free_out)
+    void* block = nullptr;
+    int kind = 0;
+    const long long rows = A.rows;
+    HostSink sink;
+    sink.alloc = [&](long long nnz, HostDst* d) -> bool {
+      const size_t bytes = sizeof(long long) * ((size_t)rows + 1) + sizeof(int) * (size_t)nnz +
+                           sizeof(double) * (size_t)nnz + 64;
+      kind = 2;
+      block = pinned_take(bytes);
+      if (!block) {
+        block = std::malloc(bytes);
+        kind = 3;
+      }
+      if (!block) return false;
+      char* p = (char*)block;
+      d->rp64 = (long long*)p;
+      p += sizeof(long long) * ((size_t)rows + 1);
+      d->ci = (int*)p;
+      d->val = (double*)(((uintptr_t)p + sizeof(int) * (size_t)nnz + 7) & ~(uintptr_t)7);
+      return true;
+    };
+    const int rc = spgemm_to_host(A, B, opt, &sink, st);
+    if (rc != kOk) {
+      if (block) {
+        if (kind == 2) pinned_give_back(block);
+        else std::free(block);
+      }
+      return rc;
+    }
+    char* p = (char*)block;
+    C->rows = rows;
+    C->cols = sink.cols;
+    C->nnz = sink.nnz;
+    C->rp = (long long*)p;
+    p += sizeof(long long) * ((size_t)rows + 1);
+    C->ci = (int*)p;
+    C->val = (double*)(((uintptr_t)p + sizeof(int) * (size_t)sink.nnz + 7) & ~(uintptr_t)7);
+    C->mem = 0;
+    C->device = opt.device;
+    C->alloc_kind = kind;
+    C->base = block;
+    return kOk;
+  }
+  if (opt.op < 0 || opt.op > 3 || opt.method < 0 || opt.method > 3) {
+    set_error("bad op or method");
+    return kErrInvalid;
+  }
+  DeviceCtx* ctx = nullptr;
+  int rc = get_ctx(opt.device, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  CK(cudaSetDevice(opt.device));
+  cudaStream_t s = opt.stream ? (cudaStream_t)opt.stream : ctx->stream;
+  const long long launches0 = kernel_launches();
+  CallStats local;
+  CallStats* stp = st ? st : &local;
+  *stp = CallStats();
+  PhaseTimer tm;
+  tm.start(opt.timing != 0 || prof_env(), s);
+  DevC dc;
+  {
+    Scratch sc(ctx, s);
+    rc = run(A, B, opt, ctx, s, sc, tm, &dc, stp, nullptr);
+    if (rc == kOk) {
       C->rp = dc.rp;
       C->ci = dc.ci;
       C->val = dc.val;
@@ -1141,83 +1326,43 @@ void compat_call(void* A_buffer, int A_rows, int A_cols, int A_nnz, void** C_buf
   opt.op = op;
   opt.method = method;
   opt.in_mem = 0;
-  opt.out_mem = 1;
+  opt.out_mem = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   opt.device = dev;
   const bool prof = prof_env();
   opt.timing = prof ? 1 : 0;
-  MatOut Cd;
-  CallStats st;
-  int rc = spgemm(A, nullptr, opt, &Cd, &st);
-  if (rc != kOk) {
-    fprintf(stderr, "[appt] %s failed: %s\n", tag, last_error());
-    return;
-  }
-  if (Cd.nnz > 0x7fffffffll) {
-    set_error("nnz(C) exceeds int32; use appt_spgemm");
-    fprintf(stderr, "[appt] %s: nnz(C)=%lld exceeds int32\n", tag, Cd.nnz);
-    free_out(&Cd);
-    return;
-  }
-  DeviceCtx* ctx = nullptr;
-  if (get_ctx(dev, &ctx)) {
-    free_out(&Cd);
-    return;
-  }
-  cudaStream_t s = (cudaStream_t)Cd.base;
-  const size_t rp_al = align8((size_t)(A_rows + 1) * 4);
-  const size_t ci_al = align8((size_t)Cd.nnz * 4);
-  const size_t total = rp_al + ci_al + (size_t)Cd.nnz * 8;
+  // C goes straight into the reference's output layout in the pinned arena
+  // [int32 row_ptr | pad8 | col_idx | pad8 | val], written while the numeric phase runs
   void* buf = nullptr;
-  if (pinned_alloc_reset(&buf, total) != 0 || !buf) {
-    set_error("pinned output allocation failed");
-    free_out(&Cd);
-    return;
-  }
-  cudaEvent_t e0 = nullptr, e1 = nullptr;
-  if (prof) {
-    cudaEventCreate(&e0);
-    cudaEventCreate(&e1);
-    cudaEventRecord(e0, s);
-  }
-  int* rp32 = nullptr;
-  bool ok = cudaMallocFromPoolAsync((void**)&rp32, sizeof(int) * ((size_t)A_rows + 1), ctx->pool, s) ==
-            cudaSuccess;
-  if (ok) {
-    narrow_rowptr(Cd.rp, rp32, (long long)A_rows + 1, s);
-    note_launches(1);
-    ok = cudaMemcpyAsync(buf, rp32, sizeof(int) * ((size_t)A_rows + 1), cudaMemcpyDeviceToHost, s) ==
-         cudaSuccess;
-    if (Cd.nnz > 0) {
-      ok = ok && cudaMemcpyAsync((char*)buf + rp_al, Cd.ci, (size_t)Cd.nnz * 4,
-                                 cudaMemcpyDeviceToHost, s) == cudaSuccess;
-      ok = ok && cudaMemcpyAsync((char*)buf + rp_al + ci_al, Cd.val, (size_t)Cd.nnz * 8,
-                                 cudaMemcpyDeviceToHost, s) == cudaSuccess;
+  bool too_big = false;
+  HostSink sink;
+  sink.alloc = [&](long long nnz, HostDst* d) -> bool {
+    if (nnz > 0x7fffffffll) {
+      too_big = true;
+      return false;
     }
-    cudaFreeAsync(rp32, s);
-  }
-  if (prof) cudaEventRecord(e1, s);
-  ok = ok && cudaStreamSynchronize(s) == cudaSuccess;
-  if (prof) {
-    float ms = 0.f;
-    cudaEventElapsedTime(&ms, e0, e1);
-    st.ms_phase[kPhD2H] += ms;
-    st.ms_total += ms;
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
-    print_prof(tag, st);
-  }
-  const long long nnz = Cd.nnz;
-  free_out(&Cd);
-  if (!ok) {
-    cudaGetLastError();
-    set_error("device-to-host copy of C failed");
-    pinned_release(buf);
+    const size_t rp_al = align8((size_t)(A_rows + 1) * 4);
+    const size_t ci_al = align8((size_t)nnz * 4);
+    if (pinned_alloc_reset(&buf, rp_al + ci_al + (size_t)nnz * 8) != 0 || !buf) {
+      buf = nullptr;
+      return false;
+    }
+    d->rp32 = (int*)buf;
+    d->ci = (int*)((char*)buf + rp_al);
+    d->val = (double*)((char*)buf + rp_al + ci_al);
+    return true;
+  };
+  CallStats st;
+  const int rc = spgemm_to_host(A, nullptr, opt, &sink, &st);
+  if (rc != kOk) {
+    if (too_big) set_error("nnz(C) exceeds int32; use appt_spgemm");
+    fprintf(stderr, "[appt] %s failed: %s\n", tag, last_error());
+    if (buf) pinned_release(buf);
     return;
   }
   *C_buffer_out = buf;
-  *C_nnz = (int)nnz;
+  *C_nnz = (int)sink.nnz;
 }
 
 void compat_build_csc(const int* d_row_ptr, const int* d_col_idx, const double* d_val, int A_rows,

@@ -104,6 +104,10 @@ size_t partition_scratch_bytes(int m, int nb);
 void partition_rows(const uint8_t* key, int m, int nb, int* out_rows, long long* bin_off,
                     void* scratch, cudaStream_t s);
 void narrow_rowptr(const long long* in, int* out, long long n, cudaStream_t s);
+// Per-bin positions of the K row blocks [k*m/K, (k+1)*m/K) in the bins' row lists:
+// sub[b * (K + 1) + k], k = 0 .. K.
+void block_bin_bounds(const int* rows, const long long* bin_off, int nb, long long m, int K,
+                      long long* sub, cudaStream_t s);
 void iota(int* out, int n, cudaStream_t s);
 
 // analyze.cu

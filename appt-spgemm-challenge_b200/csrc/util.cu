@@ -230,6 +230,32 @@ __global__ void iota_kernel(int* out, int n) {
 }
 }  // namespace
 
+namespace {
+// sub[b * (K + 1) + k] = first position in bin b's row list holding a row >= k * m / K (the
+// rows of a bin ascend), so the rows of block k that bin b holds are
+// rows[sub[b*(K+1)+k] .. sub[b*(K+1)+k+1]).
+__global__ void block_bin_bounds_kernel(const int* rows, const long long* bin_off, int nb,
+                                        long long m, int K, long long* sub) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= nb * (K + 1)) return;
+  const int b = t / (K + 1), k = t % (K + 1);
+  long long lo = bin_off[b], hi = bin_off[b + 1];
+  const long long v = (long long)k * m / K;
+  while (lo < hi) {
+    const long long mid = (lo + hi) >> 1;
+    if (rows[mid] < v) lo = mid + 1; else hi = mid;
+  }
+  sub[t] = lo;
+}
+}  // namespace
+
+void block_bin_bounds(const int* rows, const long long* bin_off, int nb, long long m, int K,
+                      long long* sub, cudaStream_t s) {
+  const int n = nb * (K + 1);
+  if (n <= 0) return;
+  block_bin_bounds_kernel<<<(n + 255) / 256, 256, 0, s>>>(rows, bin_off, nb, m, K, sub);
+}
+
 void narrow_rowptr(const long long* in, int* out, long long n, cudaStream_t s) {
   if (n <= 0) return;
   narrow_rowptr_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(in, out, n);
