@@ -63,7 +63,9 @@ struct DeviceCtx {
   int num_sms = 0;
   cudaStream_t stream = nullptr;
   cudaStream_t copy_stream = nullptr;   // device-to-host copies that overlap the numeric phase
-  cudaMemPool_t pool = nullptr;
+  cudaMemPool_t pool = nullptr;        // per-call temporaries
+  cudaMemPool_t pool_big = nullptr;    // allocations of 64 MiB and more (C, large scratch): kept
+                                       // apart so small temporaries never split their blocks
   char* stage = nullptr;   // pinned host staging for small device->host reads
   // bitmap handoff arena (symbolic -> numeric rank tier), allocated on first use and kept: calls
   // on a device are serialised by `mu` and each ends with its work complete
@@ -103,8 +105,10 @@ static int get_ctx(int device, DeviceCtx** out) {
     props.location.type = cudaMemLocationTypeDevice;
     props.location.id = device;
     CK(cudaMemPoolCreate(&c.pool, &props));
+    CK(cudaMemPoolCreate(&c.pool_big, &props));
     unsigned long long thr = ~0ull;
     CK(cudaMemPoolSetAttribute(c.pool, cudaMemPoolAttrReleaseThreshold, &thr));
+    CK(cudaMemPoolSetAttribute(c.pool_big, cudaMemPoolAttrReleaseThreshold, &thr));
     CK(cudaMallocHost((void**)&c.stage, 4096));
     c.device = device;
     c.ok = true;
@@ -126,7 +130,8 @@ struct Scratch {
     size_t bytes = count * sizeof(T);
     if (bytes == 0) bytes = 256;
     void* p = nullptr;
-    if (cudaMallocFromPoolAsync(&p, bytes, ctx->pool, s) != cudaSuccess) {
+    cudaMemPool_t pool = bytes >= (size_t(64) << 20) ? ctx->pool_big : ctx->pool;
+    if (cudaMallocFromPoolAsync(&p, bytes, pool, s) != cudaSuccess) {
       cudaGetLastError();
       failed = true;
       return nullptr;
