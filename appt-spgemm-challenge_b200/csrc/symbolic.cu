@@ -145,12 +145,34 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? APPT_SYM_MIN_BLOCKS 
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
   long long chunk_cur = 0, chunk_end = 0;   // this warp's piece of the handoff arena
-  for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
-       r += (long long)gridDim.x * WPB) {
-    const int i = rows[b0 + r];
-    const int lo = lo_arr[i];
-    const long long span = (long long)hi_arr[i] - lo + 1;
-    const long long flop = flop_arr[i];
+  // rows are software-pipelined: the next row's metadata and the id of the row after it are
+  // loaded while the current row is processed
+  const long long stride = (long long)gridDim.x * WPB;
+  long long r = (long long)blockIdx.x * WPB + warp;
+  int i_n = r < nrows ? rows[b0 + r] : 0;
+  int i_nn = r + stride < nrows ? rows[b0 + r + stride] : 0;
+  int lo_n = 0, hi_n = -1, rs_n = 0, re_n = 0;
+  long long fl_n = 0;
+  if (r < nrows) {
+    lo_n = lo_arr[i_n];
+    hi_n = hi_arr[i_n];
+    rs_n = A.rp[i_n];
+    re_n = A.rp[i_n + 1];
+    fl_n = flop_arr[i_n];
+  }
+  for (; r < nrows; r += stride) {
+    const int i = i_n, lo = lo_n, rs = rs_n, re = re_n;
+    const long long span = (long long)hi_n - lo + 1;
+    const long long flop = fl_n;
+    i_n = i_nn;
+    if (r + stride < nrows) {
+      lo_n = lo_arr[i_n];
+      hi_n = hi_arr[i_n];
+      rs_n = A.rp[i_n];
+      re_n = A.rp[i_n + 1];
+      fl_n = flop_arr[i_n];
+    }
+    if (r + 2 * stride < nrows) i_nn = rows[b0 + r + 2 * stride];
     const int W = span <= 32ll * WORDS ? bitmap_words(span) : WORDS + 1;
     if (span <= 0 || W > WORDS) {
       if (lane == 0) {
@@ -161,7 +183,6 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? APPT_SYM_MIN_BLOCKS 
     }
     for (int w = lane; w < W; w += 32) bm[w] = 0u;
     __syncwarp();
-    const int rs = A.rp[i], re = A.rp[i + 1];
     const bool bad = fill_row_bitmap_g<G>(A, B, rs, re, lo, (unsigned)span, bm);
     __syncwarp();
     int cnt = 0;
