@@ -276,6 +276,7 @@ def run_reference(args, rank: int, world: int):
                           if ln.startswith("{\"products\"")][-1])
         ms = float(np.mean(res["ms"]))
         val = 2.0 * res["products"] / (ms * 1e-3) / 1e9
+        comp = reference_compute_only_ms(r.stderr, args.steps)
         line.update({"value": val, "ms_per_step": ms, "clocks": clocks,
                      "cpu_baseline": {"value": val, "unit": UNIT, "cores": 1, "kind": "reference",
                                       "sample": "full workload through the reference's own "
@@ -284,6 +285,12 @@ def run_reference(args, rank: int, world: int):
                      "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0,
                              "d2h_bytes_per_step": 0},
                      "c_nnz": res["c_nnz"], "products": res["products"]})
+        if comp is not None:
+            line["compute_only"] = {
+                "ms_per_call": comp, "value": 2.0 * res["products"] / (comp * 1e-3) / 1e9,
+                "unit": UNIT,
+                "rule": "the reference's own cudaEvent phase profile: TOTAL(GPU) - h2d - d2h, "
+                        "mean over the timed calls"}
         line["config"]["reference"] = ("oracle/_ref/ref_spgemm (unmodified reference sources, "
                                        "sm_100a, USE_MEMPOOL=1)")
     else:
@@ -294,6 +301,28 @@ def run_reference(args, rank: int, world: int):
                              "d2h_bytes_per_step": 0}})
     print(json.dumps(line), flush=True)
     return 0
+
+
+def reference_compute_only_ms(stderr: str, calls: int):
+    """Compute-only time per call from the reference's phase profiler lines
+    ("[<tag>-prof] <phase> <ms>", one "TOTAL(GPU)" line per call): TOTAL - h2d - d2h."""
+    import re
+    pat = re.compile(r"\[(\w+)-prof\]\s+(\S.*?)\s+([0-9.]+) ms")
+    per_call, cur = [], {}
+    for ln in stderr.splitlines():
+        m = pat.search(ln)
+        if not m:
+            continue
+        name, ms = m.group(2).strip(), float(m.group(3))
+        if name == "TOTAL(GPU)":
+            per_call.append(ms - cur.get("h2d", 0.0) - cur.get("d2h", 0.0))
+            cur = {}
+        else:
+            cur[name] = cur.get(name, 0.0) + ms
+    if not per_call:
+        return None
+    tail = per_call[-calls:] if calls > 0 else per_call
+    return float(np.mean(tail))
 
 
 def cpu_baseline(A, op: str, budget_products: float = 4e10, min_seconds: float = 10.0):
