@@ -130,6 +130,9 @@ def load() -> ct.CDLL:
     lib.appt_estimate_row_nnz.argtypes = [ct.POINTER(CsrIn), ct.c_int32, ct.POINTER(Options),
                                           ct.c_void_p]
     lib.appt_estimate_row_nnz.restype = ct.c_int
+    lib.appt_estimate_row_nnz_with.argtypes = [ct.POINTER(CsrIn), ct.c_int32, ct.c_int32,
+                                               ct.POINTER(Options), ct.c_void_p]
+    lib.appt_estimate_row_nnz_with.restype = ct.c_int
     lib.appt_reference_score.argtypes = [ct.c_void_p, ct.c_int64, ct.c_int64]
     lib.appt_reference_score.restype = ct.c_double
     lib.appt_last_error.restype = ct.c_char_p
@@ -351,14 +354,21 @@ def row_products(A: Csr, B: Csr | None = None, device: int = 0) -> np.ndarray:
     return out
 
 
-def estimate_row_nnz(A: Csr, att: bool = False, device: int = 0) -> np.ndarray:
+ESTIMATORS = {"default": 0, "minhash": 1, "hll": 2}
+
+
+def estimate_row_nnz(A: Csr, att: bool = False, device: int = 0,
+                     estimator: str = "default") -> np.ndarray:
+    """The reference's per-row output-size estimate; estimator "default" follows EST_METHOD
+    like the reference, "minhash" or "hll" pick one explicitly."""
     lib = load()
     keep: list = []
     a = _host_in(A, keep)
     o = _options(device=device)
     out = np.zeros(A.rows, dtype=np.int32)
-    _check(lib.appt_estimate_row_nnz(ct.byref(a), 1 if att else 0, ct.byref(o), out.ctypes.data),
-           "appt_estimate_row_nnz")
+    _check(lib.appt_estimate_row_nnz_with(ct.byref(a), 1 if att else 0, ESTIMATORS[estimator],
+                                          ct.byref(o), out.ctypes.data),
+           "appt_estimate_row_nnz_with")
     return out
 
 

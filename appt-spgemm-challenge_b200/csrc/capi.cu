@@ -243,7 +243,15 @@ int appt_estimate_row_nnz(const appt_csr* A, int32_t att, const appt_options* op
   if (!A || !out) return APPT_ERR_INVALID;
   appt_options def;
   appt_default_options(&def);
-  return appt::estimate_row_nnz(view_of(A), att, opts_of(opt ? opt : &def), out);
+  return appt::estimate_row_nnz(view_of(A), att, 0, opts_of(opt ? opt : &def), out);
+}
+
+int appt_estimate_row_nnz_with(const appt_csr* A, int32_t att, int32_t estimator,
+                               const appt_options* opt, int32_t* out) {
+  if (!A || !out) return APPT_ERR_INVALID;
+  appt_options def;
+  appt_default_options(&def);
+  return appt::estimate_row_nnz(view_of(A), att, estimator, opts_of(opt ? opt : &def), out);
 }
 
 double appt_reference_score(const int32_t* row_ptr, int64_t rows, int64_t nnz) {

@@ -1124,7 +1124,15 @@ int row_products(const MatView& A, const MatView* B, const CallOptions& opt, lon
   return kOk;
 }
 
-int estimate_row_nnz(const MatView& A, int att, const CallOptions& opt, int* out) {
+int estimate_row_nnz(const MatView& A, int att, int estimator, const CallOptions& opt, int* out) {
+  if (estimator == 0) {
+    const char* e = std::getenv("EST_METHOD");
+    estimator = (e && std::strcmp(e, "hll") == 0) ? 2 : 1;
+  }
+  if (estimator != 1 && estimator != 2) {
+    set_error("unknown estimator");
+    return kErrInvalid;
+  }
   int rc = check_view(A, opt.in_mem, "A");
   if (rc) return rc;
   DeviceCtx* ctx = nullptr;
@@ -1153,6 +1161,11 @@ int estimate_row_nnz(const MatView& A, int att, const CallOptions& opt, int* out
   if (A.nnz < 100000) {
     launch_flop_count_i32(dA, dB, est, s);
     note_launches(m > 0 ? 1 : 0);
+  } else if (estimator == 2) {
+    unsigned char* regs = sc.get<unsigned char>((size_t)dB.rows * 128);
+    if (sc.failed) return kErrOom;
+    launch_hll_estimate(dA, dB, regs, est, ctx->num_sms, s);
+    note_launches(2);
   } else {
     unsigned* sketch = sc.get<unsigned>((size_t)dB.rows * 128);
     if (sc.failed) return kErrOom;

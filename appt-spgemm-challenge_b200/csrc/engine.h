@@ -66,7 +66,9 @@ int free_out(MatOut* C);
 int transpose(const MatView& A, const CallOptions& opt, MatOut* AT);
 int transpose_into(const MatView& A, const CallOptions& opt, int* t_rp, int* t_ci, double* t_val);
 int row_products(const MatView& A, const MatView* B, const CallOptions& opt, long long* out);
-int estimate_row_nnz(const MatView& A, int att, const CallOptions& opt, int* out);
+// estimator: 0 = the reference's default selection (EST_METHOD=hll picks HyperLogLog, else
+// MinHash), 1 = MinHash, 2 = HyperLogLog
+int estimate_row_nnz(const MatView& A, int att, int estimator, const CallOptions& opt, int* out);
 double reference_score(const int* row_ptr, long long rows, long long nnz);
 
 // spgemm.h-compatible flow: host buffer in the reference layout in, pinned host buffer in the

@@ -160,6 +160,8 @@ void launch_transpose(Csr A, long long nnz, int* t_rp, int* t_ci, double* t_val,
 // minhash.cu
 void launch_minhash_estimate(Csr A, Csr B, unsigned* sketch, int* est, int num_sms,
                              cudaStream_t s);
+void launch_hll_estimate(Csr A, Csr B, unsigned char* regs, int* est, int num_sms,
+                         cudaStream_t s);
 void launch_flop_count_i32(Csr A, Csr B, int* out, cudaStream_t s);
 
 }  // namespace appt

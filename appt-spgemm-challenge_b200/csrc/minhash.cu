@@ -1,4 +1,4 @@
-// Output-size estimator: per-partition MinHash sketch (128 partitions of 32-bit MurmurHash3
+// Output-size estimators: per-partition MinHash sketch (128 partitions of 32-bit MurmurHash3
 // minima) per B row, min-merged over the B rows an A row selects, turned into an estimate of
 // the row's distinct output columns.
 //
@@ -115,6 +115,82 @@ __global__ void __launch_bounds__(kMhWPB * 32) mh_merge_kernel(Csr A, const unsi
   }
 }
 
+// ---------------------------------------------------------------- HyperLogLog alternative
+// Reference counterpart: hll_construct_kernel / hll_merge_kernel (spgemm_kernel_hash.cu:94-240),
+// selected there by EST_METHOD=hll. Precision 7: 128 one-byte registers per B row; a column's
+// register is the low 7 bits of its MurmurHash3 and its rank the leading-zero count of the hash
+// plus one, capped at 26. A row of A takes the register-wise maximum over the B rows it selects;
+// the estimate is alpha * m^2 / sum(2^-reg) (alpha = 0.715), or m * ln(m / empty) when some
+// register is empty and the raw estimate is at most 2.5 m, then times 1.5 and snapped like the
+// MinHash estimate. sum(2^-reg) is a sum of at most 128 powers of two between 2^-26 and 1, which
+// double holds exactly, so its order does not matter.
+constexpr int kHllM = 128;
+
+__global__ void __launch_bounds__(kMhWPB * 32) hll_build_kernel(Csr B, unsigned char* regs) {
+  __shared__ unsigned rk[kMhWPB][kHllM];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long nw = (long long)gridDim.x * kMhWPB;
+  for (long long r = (long long)blockIdx.x * kMhWPB + warp; r < B.rows; r += nw) {
+    for (int t = lane; t < kHllM; t += 32) rk[warp][t] = 0u;
+    __syncwarp();
+    const int rs = B.rp[r], re = B.rp[r + 1];
+    for (int p = rs + lane; p < re; p += 32) {
+      const unsigned h = murmur3_u32((unsigned)B.ci[p]);
+      unsigned rho = (unsigned)__clz((int)h) + 1u;
+      if (rho > 26u) rho = 26u;
+      atomicMax(&rk[warp][h & (kHllM - 1)], rho);
+    }
+    __syncwarp();
+    // four registers per lane, packed into one 32-bit store
+    const unsigned packed = rk[warp][4 * lane] | (rk[warp][4 * lane + 1] << 8) |
+                            (rk[warp][4 * lane + 2] << 16) | (rk[warp][4 * lane + 3] << 24);
+    reinterpret_cast<unsigned*>(regs + (size_t)r * kHllM)[lane] = packed;
+    __syncwarp();
+  }
+}
+
+__global__ void __launch_bounds__(kMhWPB * 32) hll_merge_kernel(Csr A, const unsigned char* regs,
+                                                                int* est) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long nw = (long long)gridDim.x * kMhWPB;
+  for (long long i = (long long)blockIdx.x * kMhWPB + warp; i < A.rows; i += nw) {
+    unsigned m = 0u;
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    for (int p = rs; p < re; ++p) {
+      const int k = A.ci[p];
+      m = __vmaxu4(m, reinterpret_cast<const unsigned*>(regs + (size_t)k * kHllM)[lane]);
+    }
+    double z = 0.0;
+    int empty = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const unsigned v = (m >> (8 * q)) & 0xffu;
+      z += 1.0 / (double)(1ull << v);
+      empty += v == 0u;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      z += __shfl_down_sync(kFull, z, off);
+      empty += __shfl_down_sync(kFull, empty, off);
+    }
+    if (lane == 0) {
+      double E = 0.715 * (double)kHllM * (double)kHllM / z;
+      if (empty != 0 && E <= 2.5 * kHllM) E = (double)kHllM * log((double)kHllM / (double)empty);
+      int temp = (int)(E * 1.5);
+      if (temp < 1) temp = 1;
+      int e;
+      if (temp <= 16) {
+        e = temp;
+      } else {
+        int ht = 32;
+        while (ht < temp && ht < 16384) ht <<= 1;
+        e = ht;
+      }
+      est[i] = e;
+    }
+  }
+}
+
 __global__ void flop_count_kernel(Csr A, Csr B, int* out) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= A.rows) return;
@@ -139,6 +215,20 @@ void launch_minhash_estimate(Csr A, Csr B, unsigned* sketch, int* est, int num_s
     long long blocks = (A.rows + kMhWPB - 1) / kMhWPB;
     if (blocks > (long long)num_sms * 16) blocks = (long long)num_sms * 16;
     mh_merge_kernel<<<(unsigned)blocks, kMhWPB * 32, 0, s>>>(A, sketch, est);
+  }
+}
+
+void launch_hll_estimate(Csr A, Csr B, unsigned char* regs, int* est, int num_sms,
+                         cudaStream_t s) {
+  if (B.rows > 0) {
+    long long blocks = (B.rows + kMhWPB - 1) / kMhWPB;
+    if (blocks > (long long)num_sms * 16) blocks = (long long)num_sms * 16;
+    hll_build_kernel<<<(unsigned)blocks, kMhWPB * 32, 0, s>>>(B, regs);
+  }
+  if (A.rows > 0) {
+    long long blocks = (A.rows + kMhWPB - 1) / kMhWPB;
+    if (blocks > (long long)num_sms * 16) blocks = (long long)num_sms * 16;
+    hll_merge_kernel<<<(unsigned)blocks, kMhWPB * 32, 0, s>>>(A, regs, est);
   }
 }
 

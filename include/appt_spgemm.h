@@ -191,9 +191,19 @@ int appt_row_products(const appt_csr *A, const appt_csr *B, const appt_options *
 
 /* The reference's per-row output-size estimate (its hash-path sizing, est array): exact
  * products count when nnz(A) < 100000, else the 128-partition MinHash estimate x1.5 snapped
- * to {<=16} U {32, 64, ..., 16384}. att != 0 uses B = A^T. out has A->rows entries, host. */
+ * to {<=16} U {32, 64, ..., 16384} -- or, with EST_METHOD=hll in the environment as in the
+ * reference (src/spgemm_kernel_hash.cu:862), the HyperLogLog estimate. att != 0 uses B = A^T.
+ * out has A->rows entries, host. Replaces the est computation of hash_product
+ * (src/spgemm_kernel_hash.cu:855-912). */
 int appt_estimate_row_nnz(const appt_csr *A, int32_t att, const appt_options *opt,
                           int32_t *out);
+
+#define APPT_EST_DEFAULT 0   /* the reference's selection (EST_METHOD) */
+#define APPT_EST_MINHASH 1   /* mh_construct_kernel / mh_merge_kernel, src/spgemm_kernel_hash.cu:257-369 */
+#define APPT_EST_HLL 2       /* hll_construct_kernel / hll_merge_kernel, src/spgemm_kernel_hash.cu:94-240 */
+/* appt_estimate_row_nnz with an explicit estimator (APPT_EST_*). */
+int appt_estimate_row_nnz_with(const appt_csr *A, int32_t att, int32_t estimator,
+                               const appt_options *opt, int32_t *out);
 
 /* The reference dispatcher's score (src/spgemm_adaptive.cu:67-72) for a host row_ptr; the
  * reference picks its hash path when the score is negative. */

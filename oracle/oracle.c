@@ -221,6 +221,71 @@ void oracle_minhash_sketch(int64_t nb, const int32_t *brp, const int32_t *bci, u
   }
 }
 
+/* HyperLogLog alternative (hll_construct_kernel / hll_merge_kernel,
+ * src/spgemm_kernel_hash.cu:94-240; EST_METHOD=hll): 128 one-byte registers per B row
+ * (register = low 7 bits of the hash, rank = leading zeros + 1 capped at 26), max-merged per A
+ * row; estimate 0.715 * 128 * 128 / sum(2^-reg), or 128 * ln(128 / empty) when registers are
+ * empty and the raw estimate is at most 320; x1.5 and the same bin snap as MinHash. The sum is
+ * exact in double (powers of two between 2^-26 and 1), so its order is irrelevant. */
+static int oracle_clz32(uint32_t x) {
+  int n = 0;
+  if (x == 0) return 32;
+  while (!(x & 0x80000000u)) {
+    x <<= 1;
+    ++n;
+  }
+  return n;
+}
+
+void oracle_hll_registers(int64_t nb, const int32_t *brp, const int32_t *bci, uint8_t *regs) {
+  int nt = oracle_num_threads();
+#pragma omp parallel for schedule(static) num_threads(nt)
+  for (int64_t r = 0; r < nb; ++r) {
+    uint8_t *g = regs + r * 128;
+    for (int t = 0; t < 128; ++t) g[t] = 0;
+    for (int32_t p = brp[r]; p < brp[r + 1]; ++p) {
+      const uint32_t h = oracle_murmur3((uint32_t)bci[p]);
+      uint32_t rho = (uint32_t)oracle_clz32(h) + 1u;
+      if (rho > 26u) rho = 26u;
+      if (rho > g[h & 127u]) g[h & 127u] = (uint8_t)rho;
+    }
+  }
+}
+
+void oracle_hll_merge(int64_t m, const int32_t *arp, const int32_t *aci, const uint8_t *regs,
+                      int32_t *est) {
+  int nt = oracle_num_threads();
+#pragma omp parallel for schedule(static) num_threads(nt)
+  for (int64_t i = 0; i < m; ++i) {
+    uint8_t mx[128];
+    for (int t = 0; t < 128; ++t) mx[t] = 0;
+    for (int32_t p = arp[i]; p < arp[i + 1]; ++p) {
+      const uint8_t *g = regs + (int64_t)aci[p] * 128;
+      for (int t = 0; t < 128; ++t)
+        if (g[t] > mx[t]) mx[t] = g[t];
+    }
+    double z = 0.0;
+    int empty = 0;
+    for (int t = 0; t < 128; ++t) {
+      z += 1.0 / (double)(1ull << mx[t]);
+      empty += mx[t] == 0;
+    }
+    double E = 0.715 * 128.0 * 128.0 / z;
+    if (empty != 0 && E <= 2.5 * 128) E = 128.0 * log(128.0 / (double)empty);
+    int temp = (int)(E * 1.5);
+    if (temp < 1) temp = 1;
+    int e;
+    if (temp <= 16) {
+      e = temp;
+    } else {
+      int ht = 32;
+      while (ht < temp && ht < 16384) ht <<= 1;
+      e = ht;
+    }
+    est[i] = e;
+  }
+}
+
 /* est per A row from B's sketches: min-merge, then the reference's estimate and bin snap.
  * The sum of 1/min follows the device order: 32 lanes x 4 partitions, then a shuffle-down tree. */
 void oracle_minhash_merge(int64_t m, const int32_t *arp, const int32_t *aci,

@@ -132,6 +132,48 @@ def test_minhash_estimate_properties():
     assert np.mean(est >= exact) > 0.95
 
 
+def _hll_estimate_py(A, B):
+    """Pure-Python HyperLogLog estimate (the algorithm of the reference's hll_construct_kernel
+    / hll_merge_kernel): independent of oracle.c."""
+    import math
+    brp, bci = np.asarray(B.row_ptr, np.int64), np.asarray(B.col_idx)
+    regs = np.zeros((B.rows, 128), np.uint8)
+    for r in range(B.rows):
+        for c in bci[brp[r]:brp[r + 1]]:
+            h = murmur3_32(int(c).to_bytes(4, "little"), 1234)
+            rho = min(33 - h.bit_length(), 26) if h else 26
+            regs[r, h & 127] = max(regs[r, h & 127], rho)
+    arp, aci = np.asarray(A.row_ptr, np.int64), np.asarray(A.col_idx)
+    out = np.zeros(A.rows, np.int32)
+    for i in range(A.rows):
+        mx = regs[aci[arp[i]:arp[i + 1]]].max(axis=0) if arp[i + 1] > arp[i] else regs[0] * 0
+        z = sum(1.0 / float(1 << int(v)) for v in mx)
+        empty = int((mx == 0).sum())
+        E = 0.715 * 128.0 * 128.0 / z
+        if empty and E <= 2.5 * 128:
+            E = 128.0 * math.log(128.0 / empty)
+        t = max(int(E * 1.5), 1)
+        if t > 16:
+            ht = 32
+            while ht < t and ht < 16384:
+                ht <<= 1
+            t = ht
+        out[i] = t
+    return out
+
+
+def test_hll_estimate_matches_python_restatement():
+    A = M.stencil27(g=24)           # nnz >= 100000: the sketch path
+    est = oracle.estimate_row_nnz(A, estimator="hll")
+    rows = np.arange(0, A.rows, 97)
+    sub = M.Csr(len(rows), A.cols, np.concatenate([[0], np.cumsum(np.diff(A.row_ptr)[rows])]).astype(np.int32),
+                np.concatenate([A.col_idx[A.row_ptr[r]:A.row_ptr[r + 1]] for r in rows]),
+                np.concatenate([A.val[A.row_ptr[r]:A.row_ptr[r + 1]] for r in rows]))
+    assert np.array_equal(est[rows], _hll_estimate_py(sub, A))
+    exact = oracle.symbolic_counts(A)
+    assert np.mean(est >= exact) > 0.9
+
+
 def test_reference_score_known_choices():
     """The reference dispatcher sends the small uniform workload to merge3 and the stencil to
     hash (score sign)."""
