@@ -23,6 +23,7 @@ enum DeviceError : int {
   kErrCapacity = 2,       // a row was routed to a kernel whose capacity it exceeds
   kErrBounds = 4,         // an index check failed (write skipped)
   kErrSpin = 8,           // a bounded wait gave up
+  kErrSmallFallback = 16, // the small-problem path cannot take this input (not an error)
 };
 
 // Read-only CSR view used by kernels. `rp` values are absolute offsets into ci/val.

@@ -275,8 +275,7 @@ static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, 
   launch_analyze(A, B, upper, row_base, kMethodEsc, lanes_per_row(a_nnz, m), flop, lo, hi, key,
                  row_nnz, gst, err, sms, s);
   note_launches(m > 0 ? 1 : 0);
-  scan_exclusive(flop, foff, m, scs, s);
-  note_launches(m > 0 ? 3 : 0);
+  note_launches(scan_exclusive(flop, foff, m, scs, s));
   CK(cudaMemcpyAsync(ctx->stage, foff + m, 8, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(ctx->stage + 64, gst, sizeof(AnalyzeStats), cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(ctx->stage + 128, err, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -307,8 +306,7 @@ static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, 
   launch_esc_count(m, foff, keys, row_nnz, sms, s);
   note_launches(m > 0 ? 13 : 0);
   tm.begin(kPhScan);
-  scan_exclusive(row_nnz, crp, m, scs, s);
-  note_launches(m > 0 ? 3 : 0);
+  note_launches(scan_exclusive(row_nnz, crp, m, scs, s));
   CK(cudaMemcpyAsync(ctx->stage, crp + m, 8, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
   long long nnz;
@@ -339,11 +337,107 @@ static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, 
   return kOk;
 }
 
+// Small problems: one unbinned symbolic pass and one rank-tier launch over all rows, a handful of
+// launches instead of the binned pipeline's dozens. *fallback is set (nothing computed) when a
+// row does not fit; the caller then runs the general pipeline.
+constexpr long long kSmallRows = 65536;
+constexpr long long kSmallNnz = 1 << 21;
+
+static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
+                        cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C, CallStats* st,
+                        bool* fallback) {
+  *fallback = false;
+  const int m = A.rows;
+  const int sms = ctx->num_sms;
+  int* lo = sc.get<int>(m);
+  int* hi = sc.get<int>(m);
+  int* row_nnz = sc.get<int>(m);
+  long long* crp = sc.get<long long>((size_t)m + 1);
+  long long* boff = sc.get<long long>(2);
+  unsigned long long* tflop = sc.get<unsigned long long>(1);
+  int* err = sc.get<int>(4);
+  long long* scs = sc.get<long long>(scan_scratch_elems(m));
+  if (sc.failed) {
+    set_error("device pool allocation failed");
+    return kErrOom;
+  }
+  CK(cudaMemsetAsync(err, 0, sizeof(int) * 4, s));
+  CK(cudaMemsetAsync(tflop, 0, sizeof(unsigned long long), s));
+  const int gidx = group_index(a_nnz, m);   // B rows' average length taken from A's
+  tm.begin(kPhSymbolic);
+  launch_symbolic_small(A, B, upper, row_base, gidx, lo, hi, row_nnz, boff, tflop, err, sms, s);
+  note_launches(1);
+  tm.begin(kPhScan);
+  note_launches(scan_exclusive(row_nnz, crp, m, scs, s));
+  char* stg = ctx->stage;
+  CK(cudaMemcpyAsync(stg, crp + m, 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(stg + 8, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(stg + 16, tflop, 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  long long nnz;
+  int herr;
+  unsigned long long hflop;
+  std::memcpy(&nnz, stg, 8);
+  std::memcpy(&herr, stg + 8, sizeof(int));
+  std::memcpy(&hflop, stg + 16, 8);
+  if (herr & kErrBounds) {
+    set_error("operand index out of range (A column >= B rows)");
+    return kErrInvalid;
+  }
+  if (herr & kErrSmallFallback) {
+    *fallback = true;
+    return kOk;
+  }
+  if (herr) {
+    set_error("symbolic phase reported device error bits " + std::to_string(herr));
+    return kErrDevice;
+  }
+  int* cci = sc.get<int>(nnz);
+  double* cval = sc.get<double>(nnz);
+  if (sc.failed) {
+    set_error("device pool allocation failed for C (" + std::to_string(nnz) + " entries)");
+    return kErrOom;
+  }
+  tm.begin(kPhNumeric);
+  launch_numeric_rank_all(boff, m, gidx, A, B, lo, hi, crp, cci, cval, err, sms, s);
+  note_launches(1);
+  tm.end();
+  CK(cudaMemcpyAsync(stg + 8, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  std::memcpy(&herr, stg + 8, sizeof(int));
+  if (herr) {
+    set_error("numeric phase reported device error bits " + std::to_string(herr));
+    return kErrDevice;
+  }
+  sc.detach(crp);
+  sc.detach(cci);
+  sc.detach(cval);
+  C->rows = m;
+  C->cols = B.cols;
+  C->nnz = nnz;
+  C->rp = crp;
+  C->ci = cci;
+  C->val = cval;
+  if (st) {
+    st->products = (long long)hflop;
+    st->c_nnz = nnz;
+    st->method_used = kMethodAdaptive;
+    st->bin_rows[kNumRank8K + gidx] = m;
+  }
+  return kOk;
+}
+
 static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
                            int method, cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C,
                            CallStats* st, HostSink* sink) {
   if (method == kMethodEsc)
     return esc_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st);
+  if (method == kMethodAdaptive && A.rows > 0 && A.rows <= kSmallRows && a_nnz <= kSmallNnz &&
+      !env_flag("APPT_NO_SMALL_PATH")) {
+    bool fallback = false;
+    const int rc = small_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st, &fallback);
+    if (rc != kOk || !fallback) return rc;
+  }
   const int m = A.rows;
   const int sms = ctx->num_sms;
   constexpr int kSymMergeBin = kNumSymBins;
@@ -395,8 +489,8 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   tm.begin(kPhAnalyze);
   launch_analyze(A, B, upper, row_base, method, lanes_per_row(a_nnz, m), flop, lo, hi, symkey,
                  row_nnz, gst, err, sms, s);
-  partition_rows(symkey, m, nsb, rows_sym, boff_sym, pscr, s);
-  note_launches(m > 0 ? 7 : 0);
+  note_launches(m > 0 ? 1 : 0);   // analyze
+  note_launches(partition_rows(symkey, m, nsb, rows_sym, boff_sym, pscr, s));
 
   tm.begin(kPhSymbolic);
   if (m > 0) {
@@ -412,10 +506,10 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   }
 
   tm.begin(kPhScan);
-  scan_exclusive(row_nnz, crp, m, scs, s);
+  note_launches(scan_exclusive(row_nnz, crp, m, scs, s));
   launch_classify_numeric(A, m, method, flop, lo, hi, row_nnz, numkey, sms, s);
-  partition_rows(numkey, m, kNumNumBins, rows_num, boff_num, pscr, s);
-  note_launches(m > 0 ? 10 : 0);
+  note_launches(m > 0 ? 1 : 0);
+  note_launches(partition_rows(numkey, m, kNumNumBins, rows_num, boff_num, pscr, s));
   // with a host sink the numeric phase runs in K row blocks (rows [k*m/K, (k+1)*m/K)), each
   // bin's share of a block located by binary search in its ascending row list
   const int K = (sink && m >= 4096) ? kSinkBlocks : 1;

@@ -97,11 +97,12 @@ struct AnalyzeStats {          // device-side global statistics (atomics)
 
 // util.cu
 size_t scan_scratch_elems(long long n);
-void scan_exclusive(const int* in, long long* out, long long n, long long* scratch, cudaStream_t s);
-void scan_exclusive(const long long* in, long long* out, long long n, long long* scratch,
+// scans and partitions return the number of kernels they launched
+int scan_exclusive(const int* in, long long* out, long long n, long long* scratch, cudaStream_t s);
+int scan_exclusive(const long long* in, long long* out, long long n, long long* scratch,
                     cudaStream_t s);
 size_t partition_scratch_bytes(int m, int nb);
-void partition_rows(const uint8_t* key, int m, int nb, int* out_rows, long long* bin_off,
+int partition_rows(const uint8_t* key, int m, int nb, int* out_rows, long long* bin_off,
                     void* scratch, cudaStream_t s);
 void narrow_rowptr(const long long* in, int* out, long long n, cudaStream_t s);
 // Per-bin positions of the K row blocks [k*m/K, (k+1)*m/K) in the bins' row lists:
@@ -124,6 +125,16 @@ void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, 
                      int row_base, const int* lo, const int* hi, const long long* flop,
                      int* row_nnz, RowBitmaps handoff, int* row_counter, int* err, int num_sms,
                      cudaStream_t s);
+
+// Small problems (symbolic.cu / numeric.cu): one unbinned symbolic pass over all rows, then the
+// 9 KB rank tier over all rows; kErrSmallFallback means some row does not fit (run the general
+// pipeline instead). bin_off: 2 int64, set to {0, m} by the symbolic pass.
+void launch_symbolic_small(Csr A, Csr B, int upper, int row_base, int gidx, int* lo, int* hi,
+                           int* row_nnz, long long* bin_off, unsigned long long* total_flop,
+                           int* err, int num_sms, cudaStream_t s);
+void launch_numeric_rank_all(const long long* bin_off, long long m, int gidx, Csr A, Csr B,
+                             const int* lo, const int* hi, const long long* crp, int* cci,
+                             double* cval, int* err, int num_sms, cudaStream_t s);
 
 // numeric.cu
 // row_counter: a zeroed int (the CTA tiers take rows from it dynamically)

@@ -165,15 +165,17 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
   const int lpr = avg <= 6 ? 4 : avg <= 12 ? 8 : avg <= 24 ? 16 : 32;
   launch_analyze(dA, dB, 0, 0, kMethodAdaptive, lpr, flop, lo, hi, symkey, row_nnz, gst, err, sms,
                  s);
-  partition_rows(symkey, m, kNumSymBins + 1, rows_sym, boff_sym, pscr, s);
+  long long launched = m > 0 ? 2 : 0;   // analyze, classify
+  launched += partition_rows(symkey, m, kNumSymBins + 1, rows_sym, boff_sym, pscr, s);
   if (m > 0)
     for (int b = 0; b < kNumSymBins; ++b)
       launch_symbolic(b, rows_sym, boff_sym, dA, dB, 0, 0, lo, hi, flop, row_nnz, RowBitmaps{},
                       err + 3, err, sms, s);
-  scan_exclusive(row_nnz, crp, m, scs, s);
+  if (m > 0) launched += kNumSymBins;
+  launched += scan_exclusive(row_nnz, crp, m, scs, s);
   launch_classify_numeric(dA, m, kMethodAdaptive, flop, lo, hi, row_nnz, numkey, sms, s);
-  partition_rows(numkey, m, kNumNumBins, rows_num, boff_num, pscr, s);
-  note_launches(m > 0 ? 18 + kNumSymBins : 0);
+  launched += partition_rows(numkey, m, kNumNumBins, rows_num, boff_num, pscr, s);
+  note_launches(launched);
 
   long long nnz = 0;
   long long boff[kNumNumBins + 1];

@@ -142,12 +142,13 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
   const long long nrows = bin_off[bin + 1] - b0;
   for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
        r += (long long)gridDim.x * WPB) {
-    const int i = rows[b0 + r];
+    const int i = rows ? rows[b0 + r] : (int)(b0 + r);   // no row list: every row, in order
     const int lo = lo_arr[i];
     const long long span = (long long)hi_arr[i] - lo + 1;
     const int rs = A.rp[i], re = A.rp[i + 1];
     const long long c0 = crp[i];
     const int n = (int)(crp[i + 1] - c0);
+    if (n == 0) continue;   // (only the unbinned small-problem launch passes such rows)
     if (span <= 0 || span > 65536) {
       if (lane == 0) set_error(err, kErrCapacity);
       continue;
@@ -609,6 +610,13 @@ void run_warp_rank(int bin, int gidx, const int* rows, const long long* bin_off,
 }
 
 }  // namespace
+
+void launch_numeric_rank_all(const long long* bin_off, long long m, int gidx, Csr A, Csr B,
+                             const int* lo, const int* hi, const long long* crp, int* cci,
+                             double* cval, int* err, int num_sms, cudaStream_t s) {
+  run_warp_rank<9216, 4>(0, gidx, nullptr, bin_off, m, A, B, 0, 0, lo, hi, nullptr,
+                         RowBitmaps{}, crp, cci, cval, err, num_sms, s);
+}
 
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
                     Csr B, int upper, int row_base, const int* lo, const int* hi,

@@ -10,6 +10,7 @@
 //   * bitmap over the row's column span [lo, hi]  (one atomicOr per product, new bits counted)
 //   * open-addressing key hash with Fibonacci slots sized to >= 2 x products (never fills)
 // and rows with <= 32 products and <= 32 A entries use warp match in registers (no table).
+#include <climits>
 #include "common.cuh"
 #include "kernels.cuh"
 #include "walk.cuh"
@@ -331,7 +332,126 @@ void launch_sym_warp(int bin, const int* rows, const long long* bin_off, Csr A, 
                                               flop, row_nnz, err);
 }
 
+// Small problems: warp per row over every row of A (no binning) computes the row's column span
+// and exact count in one pass with a bitmap of at most WORDS words, writes lo / hi for the rank
+// tier, and sets kErrSmallFallback (row_nnz 0) for a row whose bitmap or rank-tier layout would
+// not fit, after which the caller runs the general pipeline. bin_off receives {0, m}.
+template <int WORDS, int WPB, int G>
+__global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int upper,
+                                                            int row_base, int* lo_arr,
+                                                            int* hi_arr, int* row_nnz,
+                                                            long long* bin_off,
+                                                            unsigned long long* total_flop,
+                                                            int* err) {
+  extern __shared__ unsigned sym_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned* bm = sym_smem + warp * WORDS;
+  const int m = A.rows;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    bin_off[0] = 0;
+    bin_off[1] = m;
+  }
+  for (long long r = (long long)blockIdx.x * WPB + warp; r < m; r += (long long)gridDim.x * WPB) {
+    const int i = (int)r;
+    const int rs = A.rp[i], re = A.rp[i + 1];
+    int lo = INT_MAX, hi = -1, bad = 0;
+    long long f = 0;
+    for (int p = rs + lane; p < re; p += 32) {
+      const int k = A.ci[p];
+      if ((unsigned)k >= (unsigned)B.rows) {
+        bad = 1;
+        continue;
+      }
+      const int b0 = B.rp[k], b1 = B.rp[k + 1];
+      if (b1 > b0) {
+        f += b1 - b0;
+        lo = min(lo, B.ci[b0]);
+        hi = max(hi, B.ci[b1 - 1]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = min(lo, __shfl_xor_sync(kFull, lo, o));
+      hi = max(hi, __shfl_xor_sync(kFull, hi, o));
+      bad |= __shfl_xor_sync(kFull, bad, o);
+      f += __shfl_xor_sync(kFull, f, o);
+    }
+    if (lane == 0 && f) atomicAdd(total_flop, (unsigned long long)f);
+    if (upper && lo < i + row_base) lo = i + row_base;
+    if (bad) {
+      if (lane == 0) {
+        set_error(err, kErrBounds);
+        row_nnz[i] = 0;
+      }
+      continue;
+    }
+    const long long span = (long long)hi - lo + 1;
+    if (lane == 0) {
+      lo_arr[i] = lo;
+      hi_arr[i] = hi;
+    }
+    if (span <= 0) {
+      if (lane == 0) row_nnz[i] = 0;
+      continue;
+    }
+    const int W = span <= 32ll * WORDS ? bitmap_words(span) : WORDS + 1;
+    if (W > WORDS || 6ll * W + 20 > kRankMaxBudget) {
+      if (lane == 0) {
+        set_error(err, kErrSmallFallback);
+        row_nnz[i] = 0;
+      }
+      continue;
+    }
+    for (int w = lane; w < W; w += 32) bm[w] = 0u;
+    __syncwarp();
+    const bool fbad = fill_row_bitmap_g<G>(A, B, rs, re, lo, (unsigned)span, bm);
+    __syncwarp();
+    int cnt = 0;
+    for (int w = lane; w < W; w += 32) cnt += __popc(bm[w]);
+    cnt = warp_sum(cnt);
+    if (lane == 0) {
+      row_nnz[i] = cnt;
+      if (fbad) set_error(err, kErrCapacity);
+      if (6ll * W + 10ll * (cnt + 1) > kRankMaxBudget) set_error(err, kErrSmallFallback);
+    }
+    __syncwarp();
+  }
+}
+
+template <int G>
+void run_sym_small(Csr A, Csr B, int upper, int row_base, int* lo, int* hi, int* row_nnz,
+                   long long* bin_off, unsigned long long* total_flop, int* err, int num_sms,
+                   cudaStream_t s) {
+  constexpr int WORDS = 1536, WPB = 8;
+  const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
+  auto kern = sym_small_kernel<WORDS, WPB, G>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_set = true;
+  }
+  long long blocks = ((long long)A.rows + WPB - 1) / WPB;
+  if (blocks > (long long)num_sms * 4) blocks = (long long)num_sms * 4;
+  if (blocks < 1) blocks = 1;
+  kern<<<(unsigned)blocks, WPB * 32, smem, s>>>(A, B, upper, row_base, lo, hi, row_nnz, bin_off,
+                                                total_flop, err);
+}
+
 }  // namespace
+
+void launch_symbolic_small(Csr A, Csr B, int upper, int row_base, int gidx, int* lo, int* hi,
+                           int* row_nnz, long long* bin_off, unsigned long long* total_flop,
+                           int* err, int num_sms, cudaStream_t s) {
+  if (gidx == 2)
+    run_sym_small<4>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, num_sms,
+                     s);
+  else if (gidx == 1)
+    run_sym_small<2>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, num_sms,
+                     s);
+  else
+    run_sym_small<1>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, num_sms,
+                     s);
+}
 
 void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
                      int row_base, const int* lo, const int* hi, const long long* flop,

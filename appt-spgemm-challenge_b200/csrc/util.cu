@@ -102,16 +102,44 @@ __global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const T* in, l
   }
 }
 
+// Inputs of at most kScanSmallMax elements: one 1024-thread block, each thread owning a
+// contiguous run; out[n] receives the total.
+constexpr int kScanSmallThreads = 1024;
+constexpr long long kScanSmallMax = 65536;
+
 template <typename T>
-void scan_impl(const T* in, long long* out, long long n, long long* scratch, cudaStream_t s) {
+__global__ void __launch_bounds__(kScanSmallThreads) scan_small_kernel(const T* in, long long n,
+                                                                       long long* out) {
+  __shared__ long long wb[kScanSmallThreads / 32 + 1];
+  const long long per = (n + kScanSmallThreads - 1) / kScanSmallThreads;
+  const long long a = (long long)threadIdx.x * per;
+  const long long b = (a + per < n) ? a + per : n;
+  long long sum = 0;
+  for (long long i = a; i < b; ++i) sum += (long long)in[i];
+  long long tot;
+  long long ex = block_excl_scan<kScanSmallThreads>(sum, wb, &tot);
+  for (long long i = a; i < b; ++i) {
+    out[i] = ex;
+    ex += (long long)in[i];
+  }
+  if (threadIdx.x == 0) out[n] = tot;
+}
+
+template <typename T>
+int scan_impl(const T* in, long long* out, long long n, long long* scratch, cudaStream_t s) {
   long long nb = (n + kScanTile - 1) / kScanTile;
   if (nb == 0) {
     cudaMemsetAsync(out, 0, sizeof(long long), s);
-    return;
+    return 0;
+  }
+  if (n <= kScanSmallMax) {
+    scan_small_kernel<T><<<1, kScanSmallThreads, 0, s>>>(in, n, out);
+    return 1;
   }
   scan_reduce_kernel<T><<<(unsigned)nb, kScanThreads, 0, s>>>(in, n, scratch);
   scan_blocksums_kernel<<<1, 1024, 0, s>>>(scratch, nb, out + n);
   scan_apply_kernel<T><<<(unsigned)nb, kScanThreads, 0, s>>>(in, n, scratch, out);
+  return 3;
 }
 
 // ---------------------------------------------------------------- stable partition
@@ -182,13 +210,13 @@ __global__ void part_binoff_kernel(const long long* offs, int nb, int ntiles, lo
 
 size_t scan_scratch_elems(long long n) { return (size_t)((n + kScanTile - 1) / kScanTile) + 1; }
 
-void scan_exclusive(const int* in, long long* out, long long n, long long* scratch,
-                    cudaStream_t s) {
-  scan_impl<int>(in, out, n, scratch, s);
+int scan_exclusive(const int* in, long long* out, long long n, long long* scratch,
+                   cudaStream_t s) {
+  return scan_impl<int>(in, out, n, scratch, s);
 }
-void scan_exclusive(const long long* in, long long* out, long long n, long long* scratch,
-                    cudaStream_t s) {
-  scan_impl<long long>(in, out, n, scratch, s);
+int scan_exclusive(const long long* in, long long* out, long long n, long long* scratch,
+                   cudaStream_t s) {
+  return scan_impl<long long>(in, out, n, scratch, s);
 }
 
 size_t partition_scratch_bytes(int m, int nb) {
@@ -198,7 +226,7 @@ size_t partition_scratch_bytes(int m, int nb) {
          sizeof(long long) * scan_scratch_elems(cells) + 256;
 }
 
-void partition_rows(const uint8_t* key, int m, int nb, int* out_rows, long long* bin_off,
+int partition_rows(const uint8_t* key, int m, int nb, int* out_rows, long long* bin_off,
                     void* scratch, cudaStream_t s) {
   int ntiles = (m + kPartTile - 1) / kPartTile;
   long long cells = (long long)ntiles * nb;
@@ -210,12 +238,13 @@ void partition_rows(const uint8_t* key, int m, int nb, int* out_rows, long long*
   long long* sc = (long long*)p;
   if (ntiles == 0) {
     cudaMemsetAsync(bin_off, 0, sizeof(long long) * (nb + 1), s);
-    return;
+    return 0;
   }
   part_count_kernel<<<ntiles, kPartThreads, 0, s>>>(key, m, nb, ntiles, counts);
-  scan_exclusive(counts, offs, cells, sc, s);
+  const int scan_launches = scan_exclusive(counts, offs, cells, sc, s);
   part_scatter_kernel<<<ntiles, kPartThreads, 0, s>>>(key, m, nb, ntiles, offs, out_rows);
   part_binoff_kernel<<<1, 32, 0, s>>>(offs, nb, ntiles, bin_off);
+  return 3 + scan_launches;
 }
 
 // ---------------------------------------------------------------- small helpers

@@ -33,6 +33,22 @@ def test_random_square(method, seed):
     check(A, method=method)
 
 
+@pytest.mark.parametrize("op", ["ab", "aat_upper"])
+@pytest.mark.parametrize("name", ["uniform8", "stencil27", "rmat", "banded"])
+def test_small_problem_path_and_general_pipeline_agree(name, op, monkeypatch):
+    """Small inputs take the unbinned small-problem path; the general binned pipeline
+    (APPT_NO_SMALL_PATH=1) must give the same C bit for bit where both use the sequential
+    rank tier, and both match the oracle."""
+    A = M.make(name, small=True)
+    C1, st1 = check(A, op=op)
+    monkeypatch.setenv("APPT_NO_SMALL_PATH", "1")
+    C2, st2 = check(A, op=op)
+    assert np.array_equal(C1.col_idx, C2.col_idx)
+    if st2["tier_rows"]["hash_block"] == st2["tier_rows"]["window"] == \
+            st2["tier_rows"]["block_rank"] == 0 and st1["tier_rows"]["rank8k"] == A.rows:
+        assert np.array_equal(C1.val, C2.val)
+
+
 @pytest.mark.parametrize("method", METHODS)
 @pytest.mark.parametrize("op", ["aat", "aat_upper"])
 def test_random_aat(method, op):
