@@ -139,7 +139,13 @@ __device__ __forceinline__ int num_bin_of(int method, long long nnz, long long f
     if (bytes <= 2304) return kNumRank2K + group_index(flop, rowlen);
     if (bytes <= 4608) return kNumRank4K + group_index(flop, rowlen);
     if (bytes <= 9216) return kNumRank8K + group_index(flop, rowlen);
-    if (nnz > 512 && span <= kWindowCols && span <= 4 * nnz) return kNumWindow;
+    // dense rows: windows of kWindowCols columns -- when the span needs several windows, only if
+    // the binary searches that restrict every B row to every window stay small next to the
+    // products
+    if (nnz > 512 && span <= 4 * nnz &&
+        (span <= kWindowCols ||
+         (long long)rowlen * ((span + kWindowCols - 1) / kWindowCols) * 64 <= flop))
+      return kNumWindow;
     if (nnz > kHashBlockSlots / 2) return kNumBlockRank;
   }
   if (nnz <= 32) return kNumHash64;

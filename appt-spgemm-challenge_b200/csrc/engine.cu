@@ -514,15 +514,19 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   // bin's share of a block located by binary search in its ascending row list
   const int K = (sink && m >= 4096) ? kSinkBlocks : 1;
   long long* bsub = nullptr;
-  int* bctr = nullptr;
+  // row counters of the CTA tiers (which take rows dynamically): one per block and bin
+  int* nctr = sc.get<int>((size_t)K * kNumNumBins);
+  if (sc.failed) {
+    set_error("device pool allocation failed");
+    return kErrOom;
+  }
+  CK(cudaMemsetAsync(nctr, 0, sizeof(int) * (size_t)K * kNumNumBins, s));
   if (K > 1) {
     bsub = sc.get<long long>((size_t)kNumNumBins * (K + 1));
-    bctr = sc.get<int>((size_t)K);
     if (sc.failed) {
       set_error("device pool allocation failed");
       return kErrOom;
     }
-    CK(cudaMemsetAsync(bctr, 0, sizeof(int) * K, s));
     block_bin_bounds(rows_num, boff_num, kNumNumBins, m, K, bsub, s);
     note_launches(1);
   }
@@ -606,7 +610,7 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
       // bin offsets of this block: bo[b], bo[b + 1] are the block's share of bin b
       const long long* bo = K > 1 ? bsub + (size_t)b * K + k : boff_num;
       const long long nr = K > 1 ? nr_all / K + 1 : nr_all;   // grid sizing only
-      int* ctr = K > 1 ? bctr + k : err + 2;
+      int* ctr = nctr + (size_t)k * kNumNumBins + b;
       if (b == kNumMerge)
         launch_merge_numeric(rows_num, bo, b, nr, A, B, upper, row_base, crp, cci, cval, err, sms,
                              s);

@@ -74,7 +74,7 @@ enum NumBin : int {
   kNumHash512,
   kNumHash1024,
   kNumHashBlock,   // CTA per row, 8192-slot table
-  kNumWindow,      // CTA per row, dense windows of 16384 columns (dense heavy rows)
+  kNumWindow,      // CTA per row, dense windows of 16384 columns (long rows, >= 1 entry / 4 cols)
   kNumBlockRank,   // CTA per row, bitmap rank over 2^20-column windows, sums in C (long rows)
   kNumMerge,       // warp per row, k-way merge of the row's B rows (merge method)
   kNumNumBins

@@ -68,7 +68,8 @@ Layout layout_for(long long m) {
   L.boff_sym = take(8 * (kMaxBins + 1));
   L.boff_num = take(8 * (kMaxBins + 1));
   L.stats = take(sizeof(AnalyzeStats));
-  L.err = take(4 * sizeof(int));
+  L.err = take((4 + kMaxBins) * sizeof(int));   // error word, counters (symbolic CTA tier at
+                                                 // [3], numeric CTA tiers at [4 + bin])
   L.scan = take(8 * scan_scratch_elems(m));
   L.part = take(partition_scratch_bytes((int)m, kMaxBins));
   L.total = o;
@@ -160,7 +161,7 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
 
   // the previous call's contents stay in the array: clear what must start at zero
   cudaMemsetAsync(gst, 0, sizeof(AnalyzeStats), s);
-  cudaMemsetAsync(err, 0, 4 * sizeof(int), s);
+  cudaMemsetAsync(err, 0, (4 + kMaxBins) * sizeof(int), s);
   const double avg = m > 0 ? (double)A.nnz / (double)m : 0.0;
   const int lpr = avg <= 6 ? 4 : avg <= 12 ? 8 : avg <= 24 ? 16 : 32;
   launch_analyze(dA, dB, 0, 0, kMethodAdaptive, lpr, flop, lo, hi, symkey, row_nnz, gst, err, sms,
@@ -209,7 +210,7 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
     const long long nr = boff[b + 1] - boff[b];
     if (nr <= 0) continue;
     launch_numeric(b, rows_num, boff_num, nr, dA, dB, 0, 0, lo, hi, flop, RowBitmaps{}, crp, cci, cval,
-                   err + 2, err, sms, s);
+                   err + 4 + b, err, sms, s);
     note_launches(1);
   }
   e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s);

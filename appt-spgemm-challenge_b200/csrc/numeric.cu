@@ -459,90 +459,96 @@ __global__ void __launch_bounds__(NT) num_block_hash_kernel(
 }
 
 // --------------------------------------------------------------------------- CTA window tier
+// Long, dense rows (at least one entry per four columns of the span, more than 512 entries): one
+// CTA per row (rows taken from a counter), the span cut into windows of WC columns. Per window:
+// a dense fp64 accumulator and a presence bitmap in shared memory, filled by the warps with
+// shared atomics (the warps share the products in pieces, load_block_chunk, walk.cuh; B rows
+// are restricted to the window by binary search when the span has several windows), then the
+// window's entries are emitted in column order at positions from one block scan of the bitmap
+// words' popcounts.
 template <int WC, int NT>
-__global__ void __launch_bounds__(NT) num_block_window_kernel(
-    const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
-    const int* lo_arr, const int* hi_arr, const long long* crp, int* cci, double* cval, int* err) {
+__global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
+    const int* rows, const long long* bin_off, int bin, Csr A, Csr B, const int* lo_arr,
+    const int* hi_arr, const long long* crp, int* cci, double* cval, int* row_counter, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
-  constexpr int W = WC / 32;
-  static_assert(W <= NT, "one bitmap word per thread in the emit scan");
-  double* acc = reinterpret_cast<double*>(num_smem);                   // [WC]
-  double* a_s = acc + WC;                                              // [NT]
-  long long* excl_s = reinterpret_cast<long long*>(a_s + NT);          // [NT]
-  unsigned* bm = reinterpret_cast<unsigned*>(excl_s + NT);             // [W]
-  int* wpre = reinterpret_cast<int*>(bm + W);                          // [W]
-  int* bs_s = wpre + W;                                                // [NT]
-  __shared__ long long sbuf[NT / 32 + 1];
-  const int tid = threadIdx.x;
+  constexpr int NW = NT / 32;
+  constexpr int WW = WC / 32;
+  static_assert(WW <= NT, "one bitmap word per thread in the emit scan");
+  double* acc = reinterpret_cast<double*>(num_smem);                      // [WC]
+  unsigned* bm = reinterpret_cast<unsigned*>(acc + WC);                   // [WW]
+  BlockChunk ch;
+  ch.a = reinterpret_cast<double*>(bm + WW);                              // [NT]
+  ch.piece_ex = reinterpret_cast<int*>(ch.a + NT);                        // [NT]
+  ch.bs = ch.piece_ex + NT;                                               // [NT]
+  ch.be = ch.bs + NT;                                                     // [NT]
+  __shared__ long long sbuf[NW + 1];
+  __shared__ long long s_row;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
-  for (long long r = blockIdx.x; r < nrows; r += gridDim.x) {
+  for (;;) {
+    if (tid == 0) s_row = atomicAdd(row_counter, 1);
+    __syncthreads();
+    const long long r = s_row;
+    if (r >= nrows) break;
     const int i = rows[b0 + r];
-    const int ig = i + row_base;
     const int lo = lo_arr[i], hi = hi_arr[i];
-    const int rs = A.rp[i], re = A.rp[i + 1];
     const long long c0 = crp[i];
     const long long n = crp[i + 1] - c0;
+    const int rs = A.rp[i], re = A.rp[i + 1];
     const bool multi = (long long)hi - lo + 1 > WC;
-    long long out = 0;
+    long long ob = 0;
     for (long long w0 = lo; w0 <= hi; w0 += WC) {
       const long long w1 = (w0 + WC < (long long)hi + 1) ? w0 + WC : (long long)hi + 1;
-      const int wspan = (int)(w1 - w0);
-      const int words = (wspan + 31) >> 5;
-      for (int s = tid; s < wspan; s += NT) acc[s] = 0.0;
+      const unsigned span = (unsigned)(w1 - w0);
+      const int words = (int)((span + 31) >> 5);
+      for (int t = tid; t < (int)span; t += NT) acc[t] = 0.0;
       for (int w = tid; w < words; w += NT) bm[w] = 0u;
-      __syncthreads();
-      for (int base = rs; base < re; base += NT) {
-        const int p = base + tid;
-        int bs = 0, be = 0;
-        double a = 0.0;
-        if (p < re) {
-          const int k = A.ci[p];
-          bs = B.rp[k];
-          be = B.rp[k + 1];
-          a = A.val[p];
-          if (multi) {
-            const int s2 = lower_bound_col(B.ci, bs, be, (int)w0);
-            be = lower_bound_col(B.ci, s2, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
-            bs = s2;
+      for (int cb = rs; cb < re; cb += NT) {
+        const int cn = (re - cb) < NT ? (re - cb) : NT;
+        const int tp = load_block_chunk<NT>(A, B, cb, re, multi, w0, w1, ch, sbuf);
+        for (int it = warp; it < tp; it += NW) {
+          const int L = search_le(ch.piece_ex, cn, it);
+          const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
+          const int q1 = (q0 + kPiece < ch.be[L]) ? q0 + kPiece : ch.be[L];
+          const double a = ch.a[L];
+          for (int q = q0 + lane; q < q1; q += 128) {
+            PieceRound pr;
+            load_piece_round<true>(B, q, q1, w0, pr);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const unsigned off = pr.off[u];
+              if (off < span) {
+                atomicAdd(acc + off, __dmul_rn(a, pr.x[u]));
+                red_or_shared_if(true, bm + (off >> 5), 1u << (off & 31));
+              }
+            }
           }
         }
-        long long total;
-        const long long ex = block_excl_scan_ll<NT>(be - bs, sbuf, &total);
-        excl_s[tid] = ex;
-        bs_s[tid] = bs;
-        a_s[tid] = a;
-        __syncthreads();
-        for (long long t = tid; t < total; t += NT) {
-          const int L = search_le(excl_s, NT, t);
-          const int q = bs_s[L] + (int)(t - excl_s[L]);
-          const int j = B.ci[q];
-          if (upper && j < ig) continue;
-          if (j < w0 || j >= w1) continue;
-          const unsigned off = (unsigned)(j - w0);
-          atomicAdd(&acc[off], a_s[L] * B.val[q]);
-          atomicOr(&bm[off >> 5], 1u << (off & 31));
-        }
         __syncthreads();
       }
-      long long cnt_w;
-      const int c = (tid < words) ? __popc(bm[tid]) : 0;
-      const long long wex = block_excl_scan_ll<NT>(c, sbuf, &cnt_w);
-      if (tid < words) wpre[tid] = (int)wex;
-      __syncthreads();
-      for (int t = tid; t < cnt_w; t += NT) {
-        const int w = search_le(wpre, words, t);
-        const int off = w * 32 + nth_set_bit(bm[w], t - wpre[w]);
-        const long long dst = out + t;
-        if (dst < n) {
-          cci[c0 + dst] = (int)(w0 + off);
-          cval[c0 + dst] = acc[off];
-        }
+      // emit: one bitmap word per thread, positions from a block scan of the popcounts
+      const unsigned bits = tid < words ? bm[tid] : 0u;
+      long long tot;
+      long long pos = block_excl_scan_ll<NT>(__popc(bits), sbuf, &tot);
+      if (ob + tot > n) {
+        if (tid == 0) set_error(err, kErrCapacity);
+        break;
       }
-      out += cnt_w;
+      unsigned rest = bits;
+      while (rest) {
+        const int b = __ffs(rest) - 1;
+        rest &= rest - 1;
+        const long long dst = c0 + ob + pos;
+        cci[dst] = (int)(w0 + 32ll * tid + b);
+        cval[dst] = acc[32 * tid + b];
+        ++pos;
+      }
       __syncthreads();
+      ob += tot;
     }
-    if (tid == 0 && out != n) set_error(err, kErrCapacity);
+    if (tid == 0 && ob != n) set_error(err, kErrCapacity);
+    __syncthreads();
   }
 }
 
@@ -687,18 +693,17 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
       break;
     }
     case kNumWindow: {
-      constexpr int NT = 512;
-      constexpr int W = kWindowCols / 32;
-      const size_t smem = (size_t)kWindowCols * 8 + (size_t)NT * (8 + 8 + 4) + (size_t)W * 8;
-      auto kern = num_block_window_kernel<kWindowCols, NT>;
+      constexpr int NT = 1024, WC = kWindowCols;
+      const size_t smem = (size_t)WC * 8 + (size_t)(WC / 32) * 4 + (size_t)NT * (8 + 12);
+      auto kern = num_block_window_kernel<WC, NT>;
       static bool attr = false;
       if (!attr) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = true;
       }
-      const int grid = occupancy_grid(kern, NT, smem, num_sms, nrows, 1);
-      kern<<<grid, NT, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, crp, cci,
-                                  cval, err);
+      const long long grid = nrows < num_sms ? nrows : num_sms;
+      kern<<<(unsigned)grid, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, crp, cci, cval,
+                                            row_counter, err);
       break;
     }
     default:
