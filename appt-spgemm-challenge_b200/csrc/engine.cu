@@ -484,6 +484,11 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
     handoff.data = ctx->harena;
     handoff.top = htop;
     handoff.capacity = kHandoffArenaWords;
+    // a smaller usable capacity (tests of the arena-full fallback)
+    if (const char* e = std::getenv("APPT_HANDOFF_WORDS")) {
+      const long long w = std::atoll(e);
+      if (w >= 0 && w < handoff.capacity) handoff.capacity = w;
+    }
   }
 
   tm.begin(kPhAnalyze);

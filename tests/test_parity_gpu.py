@@ -136,6 +136,38 @@ def test_block_rank_tier(op):
     assert st["tier_rows"]["block_rank"] > 0, st["tier_rows"]
 
 
+def test_handoff_arena_full_falls_back(monkeypatch):
+    """Rows whose symbolic bitmap finds the handoff arena full rebuild it in the numeric phase;
+    results are identical either way (and with no arena room at all)."""
+    A = M.stencil27(g=24)
+    monkeypatch.setenv("APPT_NO_SMALL_PATH", "1")
+    C0 = ap.spgemm(A)
+    for words in ("16384", "0"):
+        monkeypatch.setenv("APPT_HANDOFF_WORDS", words)
+        C1 = ap.spgemm(A)
+        assert np.array_equal(C0.row_ptr, C1.row_ptr)
+        assert np.array_equal(C0.col_idx, C1.col_idx)
+        assert np.array_equal(C0.val, C1.val)
+    R = oracle.spgemm(A)
+    assert_same_structure(C0, R)
+    assert np.array_equal(C0.val, R.val)
+
+
+def test_host_results_views_and_pinned_reuse():
+    """copy=False returns views of the library's pinned block; a released block is reused by
+    the next host result without changing it."""
+    A = M.stencil27(g=20)
+    C = ap.spgemm(A, copy=False)
+    R = oracle.spgemm(A)
+    assert_same_structure(C, R)
+    ci0 = C.col_idx.copy()
+    del C
+    for _ in range(3):
+        C2 = ap.spgemm(A, copy=False)
+        assert np.array_equal(C2.col_idx, ci0)
+        del C2
+
+
 def test_window_tier_dense_rows():
     """Rows of C with more than ~600 entries packed into at most 16384 columns take the dense
     window tier."""
