@@ -242,6 +242,10 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
   constexpr int L = 32 / G;
   const int lane = threadIdx.x & 31, grp = lane / L, sub = lane % L;
   if (!__any_sync(kFull, len > L)) {
+#ifndef APPT_RANK_PREFETCH2
+#define APPT_RANK_PREFETCH2 1
+#endif
+#if APPT_RANK_PREFETCH2
     // software pipeline: entries loaded two steps ahead, their rank looked up one step ahead
     // (the bitmap is read-only here), so a step's critical path is the accumulator update alone
     double x0, x1;
@@ -274,6 +278,32 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
       j1 = j2;
       x1 = x2;
     }
+#else
+    // software pipeline: entries and their rank one step ahead
+    double x0;
+    const int j0 = load_b_entry(B, __shfl_sync(kFull, bs, grp), __shfl_sync(kFull, len, grp),
+                                sub, lo, &x0);
+    unsigned off0 = (unsigned)(j0 - lo);
+    int r0 = rank_or(bm, pre, off0, span, n);
+    for (int t0 = 0; t0 < cnt; t0 += G) {
+      const int t1 = (t0 + G + grp) & 31;
+      double x1;
+      const int j1 = load_b_entry(B, __shfl_sync(kFull, bs, t1), __shfl_sync(kFull, len, t1),
+                                  sub, lo, &x1);
+      const double at = __shfl_sync(kFull, a, t0 + grp);
+      const double p0 = __dmul_rn(at, x0);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int pos = (G == 1 || grp == g) ? r0 : n;
+        acc[pos] = __dadd_rn(acc[pos], p0);
+        coff[pos] = (unsigned short)off0;
+        __syncwarp();
+      }
+      off0 = (unsigned)(j1 - lo);
+      r0 = rank_or(bm, pre, off0, span, n);
+      x0 = x1;
+    }
+#endif
   } else {
     for (int t0 = 0; t0 < cnt; t0 += G) {
       const int t = t0 + grp;
