@@ -62,3 +62,44 @@ def replicate(dist, tensors, src: int = 0) -> None:
 def global_row_ptr(local_row_ptr: np.ndarray, offset: int) -> np.ndarray:
     """Row pointers of a block shifted to global entry positions."""
     return np.asarray(local_row_ptr, dtype=np.int64) + int(offset)
+
+
+def gather_csr(dist, bounds, cols: int, row_ptr, col_idx, val, offsets, dst: int = 0):
+    """Assemble the sharded C on rank `dst` with point-to-point transfers: every rank passes its
+    block (row_ptr relative to the block, starting at 0, as int64; col_idx int32; val float64 --
+    torch tensors on the rank's device for NCCL, on the CPU for gloo) and `offsets` from
+    exchange_nnz. Returns (row_ptr int64, col_idx, val) of the whole C on `dst`, None elsewhere.
+    All ranks must call it."""
+    import torch
+    rank, world = dist.get_rank(), dist.get_world_size()
+    if rank != dst:
+        dist.send(row_ptr.contiguous(), dst)
+        if int(offsets[rank + 1] - offsets[rank]) > 0:
+            dist.send(col_idx.contiguous(), dst)
+            dist.send(val.contiguous(), dst)
+        return None
+    rows = int(bounds[-1])
+    total = int(offsets[-1])
+    dev = col_idx.device
+    rp = torch.empty(rows + 1, dtype=torch.int64, device=dev)
+    ci = torch.empty(total, dtype=torch.int32, device=dev)
+    va = torch.empty(total, dtype=torch.float64, device=dev)
+    for r in range(world):
+        r0, r1 = int(bounds[r]), int(bounds[r + 1])
+        e0, e1 = int(offsets[r]), int(offsets[r + 1])
+        if r == dst:
+            brp, bci, bva = row_ptr, col_idx, val
+        else:
+            brp = torch.empty(r1 - r0 + 1, dtype=torch.int64, device=dev)
+            dist.recv(brp, r)
+            bci, bva = None, None
+            if e1 > e0:
+                bci = torch.empty(e1 - e0, dtype=torch.int32, device=dev)
+                bva = torch.empty(e1 - e0, dtype=torch.float64, device=dev)
+                dist.recv(bci, r)
+                dist.recv(bva, r)
+        rp[r0:r1 + 1] = brp.to(dev) + e0
+        if e1 > e0:
+            ci[e0:e1] = bci
+            va[e0:e1] = bva
+    return rp, ci, va

@@ -69,6 +69,11 @@ def _worker(rank, world, port, op, q):
         C = oracle.spgemm(blk, B, op="ab" if op == "ab" else "ab_upper", row_base=r0)
         offs = D.exchange_nnz(dist, C.nnz, torch.device("cpu"))
         grp = D.global_row_ptr(C.row_ptr - C.row_ptr[0], offs[rank])
+        # point-to-point assembly on rank 0 (the library's gather helper)
+        got = D.gather_csr(dist, b, A.cols,
+                           torch.from_numpy(np.asarray(C.row_ptr - C.row_ptr[0], np.int64)),
+                           torch.from_numpy(np.ascontiguousarray(C.col_idx, np.int32)),
+                           torch.from_numpy(np.ascontiguousarray(C.val)), offs, dst=0)
         payload = [None] * world
         dist.all_gather_object(payload, (r0, r1, grp, C.col_idx, C.val))
         if rank == 0:
@@ -82,6 +87,10 @@ def _worker(rank, world, port, op, q):
             ok = (np.array_equal(rp, full.row_ptr) and
                   np.array_equal(np.concatenate(cols), full.col_idx) and
                   np.array_equal(np.concatenate(vals), full.val) and offs[-1] == full.nnz)
+            grp_, gci, gva = got
+            ok = ok and (np.array_equal(grp_.numpy(), full.row_ptr) and
+                         np.array_equal(gci.numpy(), full.col_idx) and
+                         np.array_equal(gva.numpy(), full.val))
             q.put(bool(ok))
     finally:
         dist.destroy_process_group()
