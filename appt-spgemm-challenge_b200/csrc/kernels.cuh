@@ -21,7 +21,7 @@ constexpr int kRankMaxBudget = 9216;    // largest per-warp shared budget of the
 // `capacity` words; each warp of the symbolic kernel takes chunks of it with one atomic on `top`
 // and places its rows' bitmaps there (logical word order). slot[i] = first word of row i's bitmap
 // / 32, or -1 (no bitmap: the arena was full, the row does not qualify, or it ran in another
-// tier). Only rows that could fit the rank tier and whose products repeat columns enough
+// tier). Only rows that could fit the rank tier and whose products outweigh their bitmap
 // (handoff_pays) are handed off. data == nullptr: no handoff at all.
 struct RowBitmaps {
   int* slot = nullptr;
@@ -37,10 +37,12 @@ __host__ __device__ __forceinline__ bool handoff_fits_rank(int bitmap_words) {
   return 6ll * bitmap_words + 20 <= kRankMaxBudget;
 }
 
-// The handoff replaces one pass over the row's products by a copy of its bitmap; it pays when
-// the products repeat columns (at least twice as many products as distinct columns).
-__host__ __device__ __forceinline__ bool handoff_pays(long long flop, long long nnz) {
-  return flop >= 2 * nnz;
+// The handoff replaces the numeric phase's pass over the row's products (about flop / 32 warp
+// steps of loads and shared atomics) by a copy of the row's W bitmap words (about W / 32
+// coalesced steps, written once by the symbolic phase); it pays unless the span is much wider
+// than the products.
+__host__ __device__ __forceinline__ bool handoff_pays(long long flop, long long words) {
+  return 3 * flop >= words;
 }
 
 // Lane groups of the warp walks (walk.cuh): a row whose B rows average <= 8 entries is walked by

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(WPB * 32) sym_warp_kernel(const int* rows, con
 
 // Warp per row, bitmap over [lo, hi] (at most WORDS words), filled with fire-and-forget shared
 // OR operations, then counted. G lane groups share the warp (rows whose B rows are short; see
-// walk.cuh). Rows that could fit the rank tier and whose products repeat columns enough
+// walk.cuh). Rows that could fit the rank tier and whose products outweigh their bitmap
 // (handoff_pays) also copy the finished bitmap out (coalesced, logical word order) into the
 // handoff arena, in chunks the warp takes with one atomic each, for the numeric rank tier.
 #ifndef APPT_SYM_MIN_BLOCKS
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? APPT_SYM_MIN_BLOCKS 
     cnt = warp_sum(cnt);
     if (__any_sync(kFull, bad) && lane == 0) set_error(err, kErrCapacity);
     if (lane == 0) row_nnz[i] = cnt;
-    if (handoff.data && handoff_fits_rank(W) && handoff_pays(flop, cnt)) {
+    if (handoff.data && handoff_fits_rank(W) && handoff_pays(flop, W)) {
       if (chunk_cur + W > chunk_end) {
         unsigned long long c = 0;
         if (lane == 0) c = atomicAdd(handoff.top, (unsigned long long)kHandoffChunkWords);
