@@ -51,7 +51,7 @@ METRIC = "SpGEMM GFLOPS (2 x intermediate products / s)"
 UNIT = "GFLOPS"
 L2_FLUSH_BYTES = 256 << 20
 E2E_MAX_C_BYTES = 16 << 30
-STREAM_BLOCK_PRODUCTS = 1 << 30
+STREAM_BLOCK_PRODUCTS = 1 << 32   # row blocks of streamed workloads: C <= 12 B x this, 48 GiB
 
 
 def _wl():
@@ -87,6 +87,8 @@ def parse_args():
     ap.add_argument("--method", default="adaptive")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--block-products", type=int, default=STREAM_BLOCK_PRODUCTS,
+                    help="products per row block of the streamed A*A^T workload")
     return ap.parse_args()
 
 
@@ -433,7 +435,7 @@ def main():
     r0, r1 = bounds[rank], bounds[rank + 1]
     my_products = int(prods[r0:r1].sum())
     if wl["op"] == "aat":
-        blocks = [r0 + b for b in cut_blocks(prods[r0:r1], STREAM_BLOCK_PRODUCTS)]
+        blocks = [r0 + b for b in cut_blocks(prods[r0:r1], args.block_products)]
     else:
         blocks = [r0, r1]
     rp_host = np.asarray(A.row_ptr, np.int64)
