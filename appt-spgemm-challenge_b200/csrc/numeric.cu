@@ -428,9 +428,17 @@ __global__ void __launch_bounds__(NT) num_block_hash_kernel(
     while (P2 < pos) P2 <<= 1;
     for (int x = (int)pos + tid; x < P2; x += NT) keys[x] = INT_MAX;
     __syncthreads();
+    // bitonic sort; a stage whose partners lie within one warp's contiguous block of P2 / NW
+    // elements runs warp-synchronously, so only the wide stages need block barriers
+    const int wb = P2 / (NT / 32);
     for (int kk = 2; kk <= P2; kk <<= 1) {
       for (int jj = kk >> 1; jj > 0; jj >>= 1) {
-        for (int x = tid; x < P2; x += NT) {
+        const bool in_warp = wb >= 32 && jj < wb;
+        if (!in_warp) __syncthreads();
+        const int x0 = in_warp ? (tid >> 5) * wb + (tid & 31) : tid;
+        const int x1 = in_warp ? ((tid >> 5) + 1) * wb : P2;
+        const int dx = in_warp ? 32 : NT;
+        for (int x = x0; x < x1; x += dx) {
           const int y = x ^ jj;
           if (y > x) {
             const int kx = keys[x], ky = keys[y];
@@ -444,9 +452,11 @@ __global__ void __launch_bounds__(NT) num_block_hash_kernel(
             }
           }
         }
-        __syncthreads();
+        if (in_warp) __syncwarp();
+        else __syncthreads();
       }
     }
+    __syncthreads();
     const int nw = pos < n ? (int)pos : n;
     if (tid == 0 && pos != n) set_error(err, kErrTableFull);
     if (overflow) set_error(err, kErrTableFull);
