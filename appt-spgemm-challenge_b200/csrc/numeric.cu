@@ -346,75 +346,78 @@ __global__ void __launch_bounds__(NT, 1) num_block_rank_kernel(
 }
 
 // --------------------------------------------------------------------------- CTA hash tier
+// Rows with 513 .. T/2 entries whose span suits neither a bitmap nor dense windows: one CTA per
+// row (rows taken from a counter), an open-addressing table of the smallest power of two >= 2 x
+// the row's exact nnz (at most T slots), filled by the warps sharing the products in pieces
+// (load_block_chunk, walk.cuh), then compacted and bitonic-sorted in shared memory.
 template <int T, int NT>
 __global__ void __launch_bounds__(NT) num_block_hash_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, int upper, int row_base,
-    const long long* crp, int* cci, double* cval, int* err) {
+    const long long* crp, int* cci, double* cval, int* row_counter, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
-  constexpr int LG = (T == 4096) ? 12 : (T == 8192) ? 13 : 14;
-  static_assert((1 << LG) == T, "table size must be 4096, 8192 or 16384");
+  constexpr int NW = NT / 32;
   double* vals = reinterpret_cast<double*>(num_smem);                  // [T]
-  double* a_s = vals + T;                                              // [NT]
-  long long* excl_s = reinterpret_cast<long long*>(a_s + NT);          // [NT]
-  int* keys = reinterpret_cast<int*>(excl_s + NT);                     // [T]
-  int* bs_s = keys + T;                                                // [NT]
-  __shared__ long long sbuf[NT / 32 + 1];
-  const int tid = threadIdx.x;
+  int* keys = reinterpret_cast<int*>(vals + T);                        // [T]
+  BlockChunk ch;
+  ch.a = reinterpret_cast<double*>(keys + T);                          // [NT]
+  ch.piece_ex = reinterpret_cast<int*>(ch.a + NT);                     // [NT]
+  ch.bs = ch.piece_ex + NT;                                            // [NT]
+  ch.be = ch.bs + NT;                                                  // [NT]
+  __shared__ long long sbuf[NW + 1];
+  __shared__ long long s_row;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
-  for (long long r = blockIdx.x; r < nrows; r += gridDim.x) {
+  for (;;) {
+    if (tid == 0) s_row = atomicAdd(row_counter, 1);
+    __syncthreads();
+    const long long r = s_row;
+    if (r >= nrows) break;
     const int i = rows[b0 + r];
-    const int ig = i + row_base;
+    const int lo = upper ? i + row_base : INT_MIN;   // upper-triangle variants drop j < i
     const int rs = A.rp[i], re = A.rp[i + 1];
     const long long c0 = crp[i];
     const int n = (int)(crp[i + 1] - c0);
-    for (int s = tid; s < T; s += NT) {
+    int lg = 6;
+    while ((1 << lg) < 2 * n && (1 << lg) < T) ++lg;
+    const int TR = 1 << lg;
+    for (int s = tid; s < TR; s += NT) {
       keys[s] = -1;
       vals[s] = 0.0;
     }
     bool overflow = false;
-    __syncthreads();
-    for (int base = rs; base < re; base += NT) {
-      const int p = base + tid;
-      int bs = 0, len = 0;
-      double a = 0.0;
-      if (p < re) {
-        const int k = A.ci[p];
-        bs = B.rp[k];
-        len = B.rp[k + 1] - bs;
-        a = A.val[p];
-      }
-      long long total;
-      const long long ex = block_excl_scan_ll<NT>(len, sbuf, &total);
-      excl_s[tid] = ex;
-      bs_s[tid] = bs;
-      a_s[tid] = a;
-      __syncthreads();
-      for (long long t = tid; t < total; t += NT) {
-        const int L = search_le(excl_s, NT, t);
-        const int q = bs_s[L] + (int)(t - excl_s[L]);
-        const int j = B.ci[q];
-        if (upper && j < ig) continue;
-        const double prod = a_s[L] * B.val[q];
-        unsigned s = hash_slot((unsigned)j, LG);
-        int probe = 0;
-        for (; probe < T; ++probe) {
-          const int old = atomicCAS(&keys[s], -1, j);
-          if (old == -1 || old == j) {
-            atomicAdd(&vals[s], prod);
-            break;
+    for (int cb = rs; cb < re; cb += NT) {
+      const int cn = (re - cb) < NT ? (re - cb) : NT;
+      const int tp = load_block_chunk<NT>(A, B, cb, re, false, 0, 0, ch, sbuf);
+      for (int it = warp; it < tp; it += NW) {
+        const int L = search_le(ch.piece_ex, cn, it);
+        const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
+        const int q1 = (q0 + kPiece < ch.be[L]) ? q0 + kPiece : ch.be[L];
+        const double a = ch.a[L];
+        for (int q = q0 + lane; q < q1; q += 32) {
+          const int j = __ldg(B.ci + q);
+          if (j < lo) continue;
+          const double prod = __dmul_rn(a, __ldg(B.val + q));
+          unsigned s = hash_slot((unsigned)j, lg);
+          int probe = 0;
+          for (; probe < TR; ++probe) {
+            const int old = atomicCAS(&keys[s], -1, j);
+            if (old == -1 || old == j) {
+              atomicAdd(&vals[s], prod);
+              break;
+            }
+            s = (s + 1) & (unsigned)(TR - 1);
           }
-          s = (s + 1) & (T - 1);
+          if (probe == TR) overflow = true;
         }
-        if (probe == T) overflow = true;
       }
       __syncthreads();
     }
     // compaction
     long long pos = 0;
-    for (int c = 0; c < T; c += NT) {
-      const int kk = keys[c + tid];
-      const double vv = vals[c + tid];
+    for (int c = 0; c < TR; c += NT) {
+      const int kk = c + tid < TR ? keys[c + tid] : -1;
+      const double vv = c + tid < TR ? vals[c + tid] : 0.0;
       long long tot;
       const long long d = block_excl_scan_ll<NT>(kk >= 0 ? 1 : 0, sbuf, &tot);
       if (kk >= 0) {
@@ -483,7 +486,8 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
   extern __shared__ __align__(16) unsigned char num_smem[];
   constexpr int NW = NT / 32;
   constexpr int WW = WC / 32;
-  static_assert(WW <= NT, "one bitmap word per thread in the emit scan");
+  constexpr int WPW = (WW + NW - 1) / NW;   // bitmap words per warp in the emit
+  static_assert(WPW <= 32, "one bitmap word per lane when counting a warp's words");
   double* acc = reinterpret_cast<double*>(num_smem);                      // [WC]
   unsigned* bm = reinterpret_cast<unsigned*>(acc + WC);                   // [WW]
   BlockChunk ch;
@@ -522,37 +526,37 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
           const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
           const int q1 = (q0 + kPiece < ch.be[L]) ? q0 + kPiece : ch.be[L];
           const double a = ch.a[L];
-          for (int q = q0 + lane; q < q1; q += 128) {
+          for (int qb = q0; qb < q1; qb += 128) {   // warp-uniform trip count
             PieceRound pr;
-            load_piece_round<true>(B, q, q1, w0, pr);
+            load_piece_round<true>(B, qb + lane, q1, w0, pr);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const unsigned off = pr.off[u];
-              if (off < span) {
-                atomicAdd(acc + off, __dmul_rn(a, pr.x[u]));
-                red_or_shared_if(true, bm + (off >> 5), 1u << (off & 31));
-              }
-            }
+            for (int u = 0; u < 4; ++u)
+              if (pr.off[u] < span) atomicAdd(acc + pr.off[u], __dmul_rn(a, pr.x[u]));
+            or_piece_round(bm, pr, span, true);   // rows of this tier are dense
           }
         }
         __syncthreads();
       }
-      // emit: one bitmap word per thread, positions from a block scan of the popcounts
-      const unsigned bits = tid < words ? bm[tid] : 0u;
+      // emit: warp wi owns words [wi * WPW, (wi + 1) * WPW) and walks them one word at a time,
+      // lane b writing bit b, so consecutive lanes store consecutive entries of C
+      const int wa = warp * WPW;
+      const int wn = words - wa < WPW ? words - wa : WPW;   // may be <= 0
+      const unsigned cnt = __reduce_add_sync(0xffffffffu, lane < wn ? __popc(bm[wa + lane]) : 0u);
       long long tot;
-      long long pos = block_excl_scan_ll<NT>(__popc(bits), sbuf, &tot);
+      const long long wpos = block_excl_scan_ll<NT>(lane == 0 ? (long long)cnt : 0ll, sbuf, &tot);
       if (ob + tot > n) {
         if (tid == 0) set_error(err, kErrCapacity);
         break;
       }
-      unsigned rest = bits;
-      while (rest) {
-        const int b = __ffs(rest) - 1;
-        rest &= rest - 1;
-        const long long dst = c0 + ob + pos;
-        cci[dst] = (int)(w0 + 32ll * tid + b);
-        cval[dst] = acc[32 * tid + b];
-        ++pos;
+      long long dst = c0 + ob + __shfl_sync(0xffffffffu, wpos, 0);
+      for (int w = wa; w < wa + wn; ++w) {
+        const unsigned bits = bm[w];
+        if ((bits >> lane) & 1u) {
+          const long long d = dst + __popc(bits & ((1u << lane) - 1u));
+          cci[d] = (int)(w0 + 32ll * w + lane);
+          cval[d] = acc[32 * w + lane];
+        }
+        dst += __popc(bits);
       }
       __syncthreads();
       ob += tot;
@@ -685,7 +689,8 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
         attr = true;
       }
       const int grid = occupancy_grid(kern, NT, smem, num_sms, nrows, 1);
-      kern<<<grid, NT, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, crp, cci, cval, err);
+      kern<<<grid, NT, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, crp, cci, cval,
+                                  row_counter, err);
       break;
     }
     case kNumBlockRank: {

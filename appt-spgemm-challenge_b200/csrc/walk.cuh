@@ -387,10 +387,40 @@ __device__ __forceinline__ void load_piece_round(const Csr& B, int q, int q1, lo
   for (int u = 0; u < 4; ++u) {
     const int qq = q + 32 * u;
     const bool v = qq < q1;
-    const int idx = v ? qq : q;   // q < q1: always a valid entry
+    const int idx = v ? qq : q1 - 1;   // the piece is not empty: q1 - 1 is always an entry
     const int j = __ldg(B.ci + idx);
     if (WITH_VAL) pr.x[u] = __ldg(B.val + idx);
     pr.off[u] = v ? (unsigned)((long long)j - w0) : 0xffffffffu;
+  }
+}
+
+// ORs the column bits of one piece round (offsets >= span are skipped) into bm. With `dense`
+// (warp-uniform; rows whose B rows are dense) the lanes' bits are first combined per word with
+// warp reductions and one lane per word issues the OR, when the round touches at most four words
+// -- fewer shared-memory atomics beside the fp64 ones of the dense-window tier; otherwise every
+// lane issues its own. All 32 lanes must call.
+__device__ __forceinline__ void or_piece_round(unsigned* bm, const PieceRound& pr, unsigned span,
+                                               bool dense) {
+  const unsigned lane = threadIdx.x & 31;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const unsigned off = pr.off[u];
+    const bool v = off < span;
+    if (dense) {
+      const unsigned w = off >> 5;
+      const unsigned wlo = __reduce_min_sync(0xffffffffu, v ? w : 0xffffffffu);
+      const unsigned whi = __reduce_max_sync(0xffffffffu, v ? w : 0u);
+      if (wlo > whi) continue;   // no lane has an entry in this round
+      if (whi - wlo < 4) {
+        for (unsigned ww = wlo; ww <= whi; ++ww) {
+          const unsigned r =
+              __reduce_or_sync(0xffffffffu, (v && w == ww) ? 1u << (off & 31) : 0u);
+          red_or_shared_if(lane == 0 && r != 0u, bm + ww, r);
+        }
+        continue;
+      }
+    }
+    red_or_shared_if(v, bm + (off >> 5), 1u << (off & 31));
   }
 }
 

@@ -72,7 +72,7 @@ def _wl():
                    "dominant": "num_warp_rank_kernel"},
         "zipf_att": {"name": "zipf_2^18x2^16_AxAT_streamed", "op": "aat", "weak": False,
                      "gen": lambda n: M.zipf_att(), "data": "Zipf(1.1) cols, U(-1,1), seed 3",
-                     "dominant": "num_block_rank_kernel"},
+                     "dominant": "num_block_window_kernel"},
     }
 
 
