@@ -427,9 +427,9 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   return kOk;
 }
 
-static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
-                           int method, cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C,
-                           CallStats* st, HostSink* sink) {
+static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long long b_nnz,
+                           int upper, int row_base, int method, cudaStream_t s, Scratch& sc,
+                           PhaseTimer& tm, DevC* C, CallStats* st, HostSink* sink) {
   if (method == kMethodEsc)
     return esc_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st);
   if (method == kMethodAdaptive && A.rows > 0 && A.rows <= kSmallRows && a_nnz <= kSmallNnz &&
@@ -498,10 +498,32 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int up
   note_launches(partition_rows(symkey, m, nsb, rows_sym, boff_sym, pscr, s));
 
   tm.begin(kPhSymbolic);
+  // bitmaps of B's dense rows for the CTA symbolic tier, when B is wide enough for that tier
+  DenseRows dense;
+  if (m > 0 && B.cols > kDenseRowsMinCols && b_nnz >= kDenseRowsMinAvg * B.rows) {
+    const long long words = ((long long)B.cols + 31) / 32;
+    long long max_rows = b_nnz * 32 / B.cols;   // rows with >= B.cols / 32 entries
+    if (max_rows > kDenseRowsMaxWords / words) max_rows = kDenseRowsMaxWords / words;
+    if (max_rows > 0) {
+      int* did = sc.get<int>(B.rows);
+      int* dlist = sc.get<int>(max_rows);
+      unsigned* dbits = sc.get<unsigned>((size_t)max_rows * words);
+      int* dcnt = sc.get<int>(1);
+      if (sc.failed) {
+        set_error("device pool allocation failed");
+        return kErrOom;
+      }
+      CK(cudaMemsetAsync(dcnt, 0, sizeof(int), s));
+      note_launches(build_dense_rows(B, did, dlist, dbits, words, (int)max_rows, dcnt, sms, s));
+      dense.id = did;
+      dense.bits = dbits;
+      dense.words = words;
+    }
+  }
   if (m > 0) {
     for (int b = 0; b < kNumSymBins; ++b)
       launch_symbolic(b, rows_sym, boff_sym, A, B, upper, row_base, lo, hi, flop, row_nnz, handoff,
-                      err + 3, err, sms, s);
+                      dense, err + 3, err, sms, s);
     note_launches(kNumSymBins);
     if (method == kMethodMerge) {
       launch_merge_count(rows_sym, boff_sym, kSymMergeBin, A, B, upper, row_base, row_nnz, err,
@@ -797,14 +819,13 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
     if (rc) return rc;
     b_nnz = A.nnz;
   }
-  (void)b_nnz;
   if (A.rows + opt.row_base >= (1ll << 31) || opt.row_base < 0) {
     set_error("row_base + rows exceeds int32");
     return kErrInvalid;
   }
   const int upper = (opt.op == kOpAATUpper || opt.op == kOpABUpper) ? 1 : 0;
-  return multiply_device(ctx, dA, dB, A.nnz, upper, (int)opt.row_base,
-                         opt.method, s, sc, tm, dc, st, sink);
+  return multiply_device(ctx, dA, dB, A.nnz, b_nnz, upper, (int)opt.row_base, opt.method, s, sc,
+                         tm, dc, st, sink);
 }
 
 // Pinned host blocks for results returned in host memory: a block released by free_out is kept

@@ -171,7 +171,7 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
   if (m > 0)
     for (int b = 0; b < kNumSymBins; ++b)
       launch_symbolic(b, rows_sym, boff_sym, dA, dB, 0, 0, lo, hi, flop, row_nnz, RowBitmaps{},
-                      err + 3, err, sms, s);
+                      DenseRows{}, err + 3, err, sms, s);
   if (m > 0) launched += kNumSymBins;
   launched += scan_exclusive(row_nnz, crp, m, scs, s);
   launch_classify_numeric(dA, m, kMethodAdaptive, flop, lo, hi, row_nnz, numkey, sms, s);

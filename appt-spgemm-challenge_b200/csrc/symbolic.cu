@@ -251,12 +251,13 @@ void launch_sym_bitmap(int bin, int gidx, const int* rows, const long long* bin_
 // columns) over [lo, hi]; rows whose span exceeds one window restrict every B row to the window
 // by binary search (B rows are sorted). The warps share the products in pieces
 // (load_block_chunk, walk.cuh), set bits with fire-and-forget shared OR operations, and the
-// window's columns are counted by popcount.
+// window's columns are counted by popcount. B rows kept as bitmaps (`dense`) are ORed in a word
+// at a time instead.
 template <int NT, int WB>
 __global__ void __launch_bounds__(NT, 1) sym_block_kernel(const int* rows, const long long* bin_off,
                                                           int bin, Csr A, Csr B, const int* lo_arr,
-                                                          const int* hi_arr, int* row_nnz,
-                                                          int* row_counter) {
+                                                          const int* hi_arr, DenseRows dense,
+                                                          int* row_nnz, int* row_counter) {
   extern __shared__ __align__(16) unsigned char sym_block_smem[];
   constexpr int NW = NT / 32;
   constexpr long long WCOLS = 32ll * WB;
@@ -266,8 +267,10 @@ __global__ void __launch_bounds__(NT, 1) sym_block_kernel(const int* rows, const
   ch.piece_ex = reinterpret_cast<int*>(ch.a + NT);               // [NT]
   ch.bs = ch.piece_ex + NT;                                      // [NT]
   ch.be = ch.bs + NT;                                            // [NT]
+  int* dlist = ch.be + NT;                                       // [NT]
   __shared__ long long sbuf[NW + 1];
   __shared__ long long s_row;
+  __shared__ int s_dcount;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
@@ -288,7 +291,8 @@ __global__ void __launch_bounds__(NT, 1) sym_block_kernel(const int* rows, const
       for (int w = tid; w < W; w += NT) bm[w] = 0u;
       for (int cb = rs; cb < re; cb += NT) {
         const int cn = (re - cb) < NT ? (re - cb) : NT;
-        const int tp = load_block_chunk<NT>(A, B, cb, re, multi, w0, w1, ch, sbuf);
+        const int tp = load_block_chunk<NT>(A, B, cb, re, multi, w0, w1, ch, sbuf, dense.id,
+                                            dlist, &s_dcount);
         for (int it = warp; it < tp; it += NW) {
           const int L = search_le(ch.piece_ex, cn, it);
           const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
@@ -302,6 +306,10 @@ __global__ void __launch_bounds__(NT, 1) sym_block_kernel(const int* rows, const
           }
         }
         __syncthreads();
+        if (dense.id && s_dcount > 0) {   // block-uniform
+          or_dense_rows<NT>(bm, W, span, w0, dense, dlist, s_dcount);
+          __syncthreads();
+        }
       }
       int c = 0;
       for (int w = tid; w < W; w += NT) c += __popc(bm[w]);
@@ -439,6 +447,49 @@ void run_sym_small(Csr A, Csr B, int upper, int row_base, int* lo, int* hi, int*
 
 }  // namespace
 
+// ---------------------------------------------------------------------------- dense B rows
+__global__ void dense_mark_kernel(Csr B, int* id, int* list, int max_rows, int* counter) {
+  const long long k = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (k >= B.rows) return;
+  const int len = B.rp[k + 1] - B.rp[k];
+  int slot = -1;
+  if (len > 0 && 32ll * len >= B.cols) {
+    slot = atomicAdd(counter, 1);
+    if (slot < max_rows)
+      list[slot] = (int)k;
+    else
+      slot = -1;
+  }
+  id[k] = slot;
+}
+
+__global__ void dense_fill_kernel(Csr B, const int* list, const int* counter, int max_rows,
+                                  unsigned* bits, long long words) {
+  const int cnt = *counter < max_rows ? *counter : max_rows;
+  for (int d = blockIdx.x; d < cnt; d += gridDim.x) {
+    const int k = list[d];
+    unsigned* row = bits + (size_t)d * words;
+    for (long long w = threadIdx.x; w < words; w += blockDim.x) row[w] = 0u;
+    __syncthreads();
+    const int e1 = B.rp[k + 1];
+    for (int e = B.rp[k] + threadIdx.x; e < e1; e += blockDim.x) {
+      const int c = B.ci[e];
+      atomicOr(row + (c >> 5), 1u << (c & 31));
+    }
+    __syncthreads();
+  }
+}
+
+int build_dense_rows(Csr B, int* id, int* list, unsigned* bits, long long words, int max_rows,
+                     int* counter, int num_sms, cudaStream_t s) {
+  if (B.rows <= 0 || max_rows <= 0) return 0;
+  dense_mark_kernel<<<(unsigned)((B.rows + 255) / 256), 256, 0, s>>>(B, id, list, max_rows,
+                                                                      counter);
+  const int grid = max_rows < 4 * num_sms ? max_rows : 4 * num_sms;
+  dense_fill_kernel<<<grid, 256, 0, s>>>(B, list, counter, max_rows, bits, words);
+  return 2;
+}
+
 void launch_symbolic_small(Csr A, Csr B, int upper, int row_base, int gidx, int* lo, int* hi,
                            int* row_nnz, long long* bin_off, unsigned long long* total_flop,
                            int* err, int num_sms, cudaStream_t s) {
@@ -455,8 +506,8 @@ void launch_symbolic_small(Csr A, Csr B, int upper, int row_base, int gidx, int*
 
 void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,
                      int row_base, const int* lo, const int* hi, const long long* flop,
-                     int* row_nnz, RowBitmaps handoff, int* row_counter, int* err, int num_sms,
-                     cudaStream_t s) {
+                     int* row_nnz, RowBitmaps handoff, DenseRows dense, int* row_counter,
+                     int* err, int num_sms, cudaStream_t s) {
   if (bin >= kSymBmS && bin < kSymBmM) {
     launch_sym_bitmap<256, 8>(bin, bin - kSymBmS, rows, bin_off, A, B, upper, row_base, lo, hi,
                               flop, row_nnz, handoff, err, num_sms, s);
@@ -487,14 +538,15 @@ void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, 
       break;
     case kSymBlock: {
       constexpr int NT = 1024;
-      const size_t smem = (size_t)kSymBlockWords * 4 + (size_t)NT * (8 + 12);
+      const size_t smem = (size_t)kSymBlockWords * 4 + (size_t)NT * (8 + 12 + 4);
       auto kern = sym_block_kernel<NT, kSymBlockWords>;
       static bool attr_set = false;
       if (!attr_set) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr_set = true;
       }
-      kern<<<num_sms, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, row_nnz, row_counter);
+      kern<<<num_sms, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, dense, row_nnz,
+                                     row_counter);
       break;
     }
     default:

@@ -12,6 +12,7 @@
 // predicated loads and updates.
 #pragma once
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace appt {
 
@@ -342,34 +343,63 @@ struct BlockChunk {   // one chunk of up to NT A entries of a row, in shared mem
 };
 
 // Loads A entries [cb, cb + NT) of the row (segments restricted to [w0, w1) when `multi`) and
-// returns the number of pieces. Contains barriers.
+// returns the number of pieces. With `dense_id`, entries whose B row has a bitmap get no pieces
+// and their bitmap indices are listed in dlist[0 .. *dcount) instead. Contains barriers.
 template <int NT>
 __device__ __forceinline__ int load_block_chunk(const Csr& A, const Csr& B, int cb, int re,
                                                 bool multi, long long w0, long long w1,
-                                                BlockChunk ch, long long* sbuf) {
+                                                BlockChunk ch, long long* sbuf,
+                                                const int* dense_id = nullptr,
+                                                int* dlist = nullptr, int* dcount = nullptr) {
   const int tid = threadIdx.x;
   const int p = cb + tid;
-  int bs = 0, be = 0;
+  int bs = 0, be = 0, did = -1;
   double a = 0.0;
+  if (dense_id && tid == 0) *dcount = 0;   // readers of the previous list passed a barrier
   if (p < re) {
     const int k = __ldg(A.ci + p);
-    bs = __ldg(B.rp + k);
-    be = __ldg(B.rp + k + 1);
-    a = __ldg(A.val + p);
-    if (multi) {
-      bs = lower_bound_col(B.ci, bs, be, (int)w0);
-      be = lower_bound_col(B.ci, bs, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
+    if (dense_id) did = __ldg(dense_id + k);
+    if (did < 0) {
+      bs = __ldg(B.rp + k);
+      be = __ldg(B.rp + k + 1);
+      a = __ldg(A.val + p);
+      if (multi) {
+        bs = lower_bound_col(B.ci, bs, be, (int)w0);
+        be = lower_bound_col(B.ci, bs, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
+      }
     }
   }
   const int pieces = (be - bs + kPiece - 1) / kPiece;
   long long tot;
-  const long long ex = block_excl_scan_ll<NT>(pieces, sbuf, &tot);
+  const long long ex = block_excl_scan_ll<NT>(pieces, sbuf, &tot);   // orders the reset above
+  if (did >= 0) dlist[atomicAdd(dcount, 1)] = did;
   ch.piece_ex[tid] = (int)ex;
   ch.bs[tid] = bs;
   ch.be[tid] = be;
   ch.a[tid] = a;
   __syncthreads();
   return (int)tot;
+}
+
+// ORs the words of window [w0, w0 + span) of the listed dense B rows into bm (W words; thread
+// per word, plain read-modify-write: no other writer may run concurrently).
+template <int NT>
+__device__ __forceinline__ void or_dense_rows(unsigned* bm, int W, unsigned span, long long w0,
+                                              const DenseRows& dense, const int* dlist, int nd) {
+  const long long g0 = w0 >> 5;
+  const int sh = (int)(w0 & 31);
+  for (int w = threadIdx.x; w < W; w += NT) {
+    const long long g = g0 + w;
+    unsigned acc = 0u;
+    for (int d = 0; d < nd; ++d) {
+      const unsigned* row = dense.bits + (size_t)dlist[d] * dense.words;
+      const unsigned x0 = __ldg(row + g);
+      const unsigned x1 = g + 1 < dense.words ? __ldg(row + g + 1) : 0u;
+      acc |= __funnelshift_r(x0, x1, sh);
+    }
+    if (w == W - 1 && (span & 31u)) acc &= (1u << (span & 31u)) - 1u;
+    bm[w] |= acc;
+  }
 }
 
 // Entries [q0, q1) of a B row, four rounds of 32 per lane-step with all loads issued before any

@@ -196,6 +196,30 @@ def test_block_rank_multiwindow():
     assert st["tier_rows"]["block_rank"] > 0, st["tier_rows"]
 
 
+@pytest.mark.parametrize("op", ["ab", "ab_upper"])
+def test_dense_b_rows_in_cta_symbolic_tier(op):
+    """B rows with at least one entry per 32 columns are kept as bitmaps and ORed into the CTA
+    symbolic tier's windows a word at a time. The rows of C span more than 2^20 columns (several
+    windows, starts not aligned to 32), and A's rows mix dense and sparse B rows."""
+    rng = np.random.default_rng(11)
+    k, cols = 1024, (1 << 20) + 40000
+    brows = [np.unique(rng.integers(0, cols, cols // 16 if r % 128 == 3 else 100))
+             for r in range(k)]
+    brp = np.zeros(k + 1, np.int64)
+    brp[1:] = np.cumsum([len(r) for r in brows])
+    bci = np.concatenate(brows).astype(np.int32)
+    B = M.Csr(k, cols, brp.astype(np.int32), bci, rng.uniform(-1, 1, bci.size))
+    m = 160
+    arows = [np.unique(np.concatenate([rng.integers(0, k, 11), [128 * (r % 8) + 3]]))
+             if r % 5 else np.unique(rng.integers(0, k, 12)) for r in range(m)]
+    arp = np.zeros(m + 1, np.int64)
+    arp[1:] = np.cumsum([len(r) for r in arows])
+    aci = np.concatenate(arows).astype(np.int32)
+    A = M.Csr(m, k, arp.astype(np.int32), aci, rng.uniform(-1, 1, aci.size))
+    C, st = check(A, B, op=op)
+    assert st["tier_rows"]["block_rank"] > 0, st["tier_rows"]
+
+
 @pytest.mark.parametrize("method", ["adaptive", "hash", "esc"])
 @pytest.mark.parametrize("name", ["uniform8", "stencil27", "banded", "random"])
 def test_sequential_tiers_are_bit_exact(name, method):
