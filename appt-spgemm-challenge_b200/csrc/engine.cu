@@ -501,23 +501,26 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
   // bitmaps of B's dense rows for the CTA symbolic tier, when B is wide enough for that tier
   DenseRows dense;
   if (m > 0 && B.cols > kDenseRowsMinCols && b_nnz >= kDenseRowsMinAvg * B.rows) {
-    const long long words = ((long long)B.cols + 31) / 32;
+    const long long stride = ((long long)B.cols + 31) / 32 + 1;
     long long max_rows = b_nnz * 32 / B.cols;   // rows with >= B.cols / 32 entries
-    if (max_rows > kDenseRowsMaxWords / words) max_rows = kDenseRowsMaxWords / words;
+    if (max_rows > kDenseRowsMaxWords / (2 * stride)) max_rows = kDenseRowsMaxWords / (2 * stride);
     if (max_rows > 0) {
       int* did = sc.get<int>(B.rows);
       int* dlist = sc.get<int>(max_rows);
-      unsigned* dbits = sc.get<unsigned>((size_t)max_rows * words);
+      unsigned* dbits = sc.get<unsigned>((size_t)max_rows * stride);
+      unsigned* dpre = sc.get<unsigned>((size_t)max_rows * stride);
       int* dcnt = sc.get<int>(1);
       if (sc.failed) {
         set_error("device pool allocation failed");
         return kErrOom;
       }
       CK(cudaMemsetAsync(dcnt, 0, sizeof(int), s));
-      note_launches(build_dense_rows(B, did, dlist, dbits, words, (int)max_rows, dcnt, sms, s));
+      note_launches(
+          build_dense_rows(B, did, dlist, dbits, dpre, stride, (int)max_rows, dcnt, sms, s));
       dense.id = did;
       dense.bits = dbits;
-      dense.words = words;
+      dense.pre = dpre;
+      dense.stride = stride;
     }
   }
   if (m > 0) {
@@ -642,8 +645,8 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
         launch_merge_numeric(rows_num, bo, b, nr, A, B, upper, row_base, crp, cci, cval, err, sms,
                              s);
       else
-        launch_numeric(b, rows_num, bo, nr, A, B, upper, row_base, lo, hi, flop, handoff, crp,
-                       cci, cval, ctr, err, sms, s);
+        launch_numeric(b, rows_num, bo, nr, A, B, upper, row_base, lo, hi, flop, handoff, dense,
+                       crp, cci, cval, ctr, err, sms, s);
       note_launches(1);
     }
     if (sink) {

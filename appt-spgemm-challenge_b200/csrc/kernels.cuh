@@ -48,18 +48,22 @@ __host__ __device__ __forceinline__ bool handoff_pays(long long flop, long long 
 // B rows kept a second time as column bitmaps -- rows with at least one entry per 32 columns of
 // B -- so that the CTA walks OR whole words of a window from them instead of one bit per entry.
 // id == nullptr: none.
+// Each kept row also has the exclusive popcount prefix of its words, so the entries of a column
+// range are found in O(1): rank(c) = pre[c / 32] + popc(bits[c / 32] & below(c % 32)). Rows are
+// `stride` = ceil(B.cols / 32) + 1 words apart (the extra word makes rank(B.cols) valid).
 struct DenseRows {
   const int* id = nullptr;          // [B.rows] index of the row's bitmap, -1 when it has none
-  const unsigned* bits = nullptr;   // [rows kept][words]
-  long long words = 0;              // ceil(B.cols / 32)
+  const unsigned* bits = nullptr;   // [rows kept][stride]
+  const unsigned* pre = nullptr;    // [rows kept][stride]
+  long long stride = 0;
 };
 
-// Only the CTA symbolic tier (spans beyond the warp tiers' 4096 words) uses them, so they are
-// built only when B is that wide, and only when B's rows average enough entries for some row to
+// The CTA tiers with window spans beyond the warp tiers' 4096 words use them, so they are built
+// only when B is that wide, and only when B's rows average enough entries for some row to
 // qualify often enough to pay for the build.
 constexpr long long kDenseRowsMinCols = 32ll * 4096;
 constexpr long long kDenseRowsMinAvg = 64;
-constexpr long long kDenseRowsMaxWords = 1ll << 26;   // 256 MB of bitmaps at most
+constexpr long long kDenseRowsMaxWords = 1ll << 27;   // 512 MB of bitmaps and prefixes at most
 
 // Lane groups of the warp walks (walk.cuh): a row whose B rows average <= 8 entries is walked by
 // 4 groups of 8 lanes, <= 16 by 2 groups of 16, longer by the whole warp. Tiers that walk
@@ -143,10 +147,10 @@ void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, 
                      int row_base, const int* lo, const int* hi, const long long* flop,
                      int* row_nnz, RowBitmaps handoff, DenseRows dense, int* row_counter,
                      int* err, int num_sms, cudaStream_t s);
-// Bitmaps of B's dense rows (at most max_rows of them; counter: a zeroed int). Returns the
-// number of kernels launched.
-int build_dense_rows(Csr B, int* id, int* list, unsigned* bits, long long words, int max_rows,
-                     int* counter, int num_sms, cudaStream_t s);
+// Bitmaps and prefixes of B's dense rows (at most max_rows of them; counter: a zeroed int).
+// Returns the number of kernels launched.
+int build_dense_rows(Csr B, int* id, int* list, unsigned* bits, unsigned* pre, long long stride,
+                     int max_rows, int* counter, int num_sms, cudaStream_t s);
 
 // Small problems (symbolic.cu / numeric.cu): one unbinned symbolic pass over all rows, then the
 // 9 KB rank tier over all rows; kErrSmallFallback means some row does not fit (run the general
@@ -162,8 +166,9 @@ void launch_numeric_rank_all(const long long* bin_off, long long m, int gidx, Cs
 // row_counter: a zeroed int (the CTA tiers take rows from it dynamically)
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows_host,
                     Csr A, Csr B, int upper, int row_base, const int* lo, const int* hi,
-                    const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
-                    double* cval, int* row_counter, int* err, int num_sms, cudaStream_t s);
+                    const long long* flop, RowBitmaps handoff, DenseRows dense,
+                    const long long* crp, int* cci, double* cval, int* row_counter, int* err,
+                    int num_sms, cudaStream_t s);
 
 // merge.cu
 void launch_merge_count(const int* rows, const long long* bin_off, int bin, Csr A, Csr B,

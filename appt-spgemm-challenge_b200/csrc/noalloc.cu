@@ -209,8 +209,8 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
   for (int b = 0; b < kNumNumBins; ++b) {
     const long long nr = boff[b + 1] - boff[b];
     if (nr <= 0) continue;
-    launch_numeric(b, rows_num, boff_num, nr, dA, dB, 0, 0, lo, hi, flop, RowBitmaps{}, crp, cci, cval,
-                   err + 4 + b, err, sms, s);
+    launch_numeric(b, rows_num, boff_num, nr, dA, dB, 0, 0, lo, hi, flop, RowBitmaps{},
+                   DenseRows{}, crp, cci, cval, err + 4 + b, err, sms, s);
     note_launches(1);
   }
   e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s);

@@ -482,11 +482,13 @@ __global__ void __launch_bounds__(NT) num_block_hash_kernel(
 template <int WC, int NT>
 __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, const int* lo_arr,
-    const int* hi_arr, const long long* crp, int* cci, double* cval, int* row_counter, int* err) {
+    const int* hi_arr, DenseRows dense, const long long* crp, int* cci, double* cval,
+    int* row_counter, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
   constexpr int NW = NT / 32;
   constexpr int WW = WC / 32;
   constexpr int WPW = (WW + NW - 1) / NW;   // bitmap words per warp in the emit
+  constexpr int SUB = WC / NW;              // columns per warp in the dense-row products
   static_assert(WPW <= 32, "one bitmap word per lane when counting a warp's words");
   double* acc = reinterpret_cast<double*>(num_smem);                      // [WC]
   unsigned* bm = reinterpret_cast<unsigned*>(acc + WC);                   // [WW]
@@ -495,8 +497,10 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
   ch.piece_ex = reinterpret_cast<int*>(ch.a + NT);                        // [NT]
   ch.bs = ch.piece_ex + NT;                                               // [NT]
   ch.be = ch.bs + NT;                                                     // [NT]
+  int* dlist = ch.be + NT;                                                // [NT]
   __shared__ long long sbuf[NW + 1];
   __shared__ long long s_row;
+  __shared__ int s_dcount;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
@@ -520,7 +524,8 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
       for (int w = tid; w < words; w += NT) bm[w] = 0u;
       for (int cb = rs; cb < re; cb += NT) {
         const int cn = (re - cb) < NT ? (re - cb) : NT;
-        const int tp = load_block_chunk<NT>(A, B, cb, re, multi, w0, w1, ch, sbuf);
+        const int tp = load_block_chunk<NT>(A, B, cb, re, multi, w0, w1, ch, sbuf, dense.id,
+                                            dlist, &s_dcount);
         for (int it = warp; it < tp; it += NW) {
           const int L = search_le(ch.piece_ex, cn, it);
           const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
@@ -536,6 +541,45 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
           }
         }
         __syncthreads();
+        const int nd = dense.id ? s_dcount : 0;
+        if (nd > 0) {   // block-uniform
+          // B rows kept as bitmaps: their bits a word at a time, and their products by column
+          // slices -- warp wi owns columns [w0 + wi * SUB, w0 + (wi + 1) * SUB) and adds every
+          // listed row's entries there in list order with plain shared-memory updates (no other
+          // warp writes those sums)
+          or_dense_rows<NT>(bm, words, span, w0, dense, ch, dlist, nd);
+          const long long c_lo = w0 + (long long)warp * SUB;
+          const long long c_hi = c_lo + SUB < w1 ? c_lo + SUB : w1;
+          if (c_lo < c_hi) {
+            for (int d0 = 0; d0 < nd; d0 += 32) {
+              int s0 = 0, s1 = 0;
+              double ad = 0.0;
+              if (d0 + lane < nd) {
+                const int t = dlist[d0 + lane];
+                const int did = ch.be[t];
+                s0 = ch.bs[t] + dense_rank(dense, did, c_lo);
+                s1 = ch.bs[t] + dense_rank(dense, did, c_hi);
+                ad = ch.a[t];
+              }
+              const int cnt = nd - d0 < 32 ? nd - d0 : 32;
+              for (int j = 0; j < cnt; ++j) {
+                const int q0 = __shfl_sync(0xffffffffu, s0, j);
+                const int q1 = __shfl_sync(0xffffffffu, s1, j);
+                const double a = __shfl_sync(0xffffffffu, ad, j);
+                for (int qb = q0; qb < q1; qb += 128) {
+                  PieceRound pr;
+                  load_piece_round<true>(B, qb + lane, q1, w0, pr);
+#pragma unroll
+                  for (int u = 0; u < 4; ++u)
+                    if (pr.off[u] < span)
+                      acc[pr.off[u]] = __dadd_rn(acc[pr.off[u]], __dmul_rn(a, pr.x[u]));
+                }
+                __syncwarp();   // the next row's entries may hit these columns in other lanes
+              }
+            }
+          }
+          __syncthreads();
+        }
       }
       // emit: warp wi owns words [wi * WPW, (wi + 1) * WPW) and walks them one word at a time,
       // lane b writing bit b, so consecutive lanes store consecutive entries of C
@@ -640,8 +684,9 @@ void launch_numeric_rank_all(const long long* bin_off, long long m, int gidx, Cs
 
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,
                     Csr B, int upper, int row_base, const int* lo, const int* hi,
-                    const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
-                    double* cval, int* row_counter, int* err, int num_sms, cudaStream_t s) {
+                    const long long* flop, RowBitmaps handoff, DenseRows dense,
+                    const long long* crp, int* cci, double* cval, int* row_counter, int* err,
+                    int num_sms, cudaStream_t s) {
   if (nrows <= 0) return;
   if (bin >= kNumRank2K && bin < kNumRank2K + 3) {
     run_warp_rank<2304, 8>(bin, bin - kNumRank2K, rows, bin_off, nrows, A, B, upper, row_base, lo,
@@ -709,7 +754,7 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
     }
     case kNumWindow: {
       constexpr int NT = 1024, WC = kWindowCols;
-      const size_t smem = (size_t)WC * 8 + (size_t)(WC / 32) * 4 + (size_t)NT * (8 + 12);
+      const size_t smem = (size_t)WC * 8 + (size_t)(WC / 32) * 4 + (size_t)NT * (8 + 12 + 4);
       auto kern = num_block_window_kernel<WC, NT>;
       static bool attr = false;
       if (!attr) {
@@ -717,8 +762,8 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
         attr = true;
       }
       const long long grid = nrows < num_sms ? nrows : num_sms;
-      kern<<<(unsigned)grid, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, crp, cci, cval,
-                                            row_counter, err);
+      kern<<<(unsigned)grid, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, dense, crp, cci,
+                                            cval, row_counter, err);
       break;
     }
     default:

@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(NT, 1) sym_block_kernel(const int* rows, const
         }
         __syncthreads();
         if (dense.id && s_dcount > 0) {   // block-uniform
-          or_dense_rows<NT>(bm, W, span, w0, dense, dlist, s_dcount);
+          or_dense_rows<NT>(bm, W, span, w0, dense, ch, dlist, s_dcount);
           __syncthreads();
         }
       }
@@ -463,13 +463,17 @@ __global__ void dense_mark_kernel(Csr B, int* id, int* list, int max_rows, int* 
   id[k] = slot;
 }
 
-__global__ void dense_fill_kernel(Csr B, const int* list, const int* counter, int max_rows,
-                                  unsigned* bits, long long words) {
+__global__ void __launch_bounds__(256) dense_fill_kernel(Csr B, const int* list,
+                                                         const int* counter, int max_rows,
+                                                         unsigned* bits, unsigned* pre,
+                                                         long long stride) {
+  __shared__ long long sbuf[256 / 32 + 1];
   const int cnt = *counter < max_rows ? *counter : max_rows;
+  const int per = (int)((stride + 255) / 256);   // words per thread in the prefix
   for (int d = blockIdx.x; d < cnt; d += gridDim.x) {
     const int k = list[d];
-    unsigned* row = bits + (size_t)d * words;
-    for (long long w = threadIdx.x; w < words; w += blockDim.x) row[w] = 0u;
+    unsigned* row = bits + (size_t)d * stride;
+    for (long long w = threadIdx.x; w < stride; w += blockDim.x) row[w] = 0u;
     __syncthreads();
     const int e1 = B.rp[k + 1];
     for (int e = B.rp[k] + threadIdx.x; e < e1; e += blockDim.x) {
@@ -477,16 +481,28 @@ __global__ void dense_fill_kernel(Csr B, const int* list, const int* counter, in
       atomicOr(row + (c >> 5), 1u << (c & 31));
     }
     __syncthreads();
+    const long long wa = (long long)threadIdx.x * per;
+    const long long wb = wa + per < stride ? wa + per : stride;
+    long long c = 0;
+    for (long long w = wa; w < wb; ++w) c += __popc(row[w]);
+    long long tot;
+    long long run = block_excl_scan_ll<256>(c, sbuf, &tot);
+    unsigned* prow = pre + (size_t)d * stride;
+    for (long long w = wa; w < wb; ++w) {
+      prow[w] = (unsigned)run;
+      run += __popc(row[w]);
+    }
+    __syncthreads();
   }
 }
 
-int build_dense_rows(Csr B, int* id, int* list, unsigned* bits, long long words, int max_rows,
-                     int* counter, int num_sms, cudaStream_t s) {
+int build_dense_rows(Csr B, int* id, int* list, unsigned* bits, unsigned* pre, long long stride,
+                     int max_rows, int* counter, int num_sms, cudaStream_t s) {
   if (B.rows <= 0 || max_rows <= 0) return 0;
   dense_mark_kernel<<<(unsigned)((B.rows + 255) / 256), 256, 0, s>>>(B, id, list, max_rows,
                                                                       counter);
   const int grid = max_rows < 4 * num_sms ? max_rows : 4 * num_sms;
-  dense_fill_kernel<<<grid, 256, 0, s>>>(B, list, counter, max_rows, bits, words);
+  dense_fill_kernel<<<grid, 256, 0, s>>>(B, list, counter, max_rows, bits, pre, stride);
   return 2;
 }
 

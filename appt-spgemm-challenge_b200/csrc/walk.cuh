@@ -343,8 +343,9 @@ struct BlockChunk {   // one chunk of up to NT A entries of a row, in shared mem
 };
 
 // Loads A entries [cb, cb + NT) of the row (segments restricted to [w0, w1) when `multi`) and
-// returns the number of pieces. With `dense_id`, entries whose B row has a bitmap get no pieces
-// and their bitmap indices are listed in dlist[0 .. *dcount) instead. Contains barriers.
+// returns the number of pieces. With `dense_id`, entries whose B row has a bitmap get no pieces:
+// their chunk indices are listed in dlist[0 .. *dcount), with bs = the B row's first entry and
+// be = its bitmap index. Contains barriers.
 template <int NT>
 __device__ __forceinline__ int load_block_chunk(const Csr& A, const Csr& B, int cb, int re,
                                                 bool multi, long long w0, long long w1,
@@ -359,20 +360,22 @@ __device__ __forceinline__ int load_block_chunk(const Csr& A, const Csr& B, int 
   if (p < re) {
     const int k = __ldg(A.ci + p);
     if (dense_id) did = __ldg(dense_id + k);
+    bs = __ldg(B.rp + k);
+    a = __ldg(A.val + p);
     if (did < 0) {
-      bs = __ldg(B.rp + k);
       be = __ldg(B.rp + k + 1);
-      a = __ldg(A.val + p);
       if (multi) {
         bs = lower_bound_col(B.ci, bs, be, (int)w0);
         be = lower_bound_col(B.ci, bs, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
       }
+    } else {
+      be = did;
     }
   }
-  const int pieces = (be - bs + kPiece - 1) / kPiece;
+  const int pieces = did < 0 ? (be - bs + kPiece - 1) / kPiece : 0;
   long long tot;
   const long long ex = block_excl_scan_ll<NT>(pieces, sbuf, &tot);   // orders the reset above
-  if (did >= 0) dlist[atomicAdd(dcount, 1)] = did;
+  if (did >= 0) dlist[atomicAdd(dcount, 1)] = tid;
   ch.piece_ex[tid] = (int)ex;
   ch.bs[tid] = bs;
   ch.be[tid] = be;
@@ -381,21 +384,27 @@ __device__ __forceinline__ int load_block_chunk(const Csr& A, const Csr& B, int 
   return (int)tot;
 }
 
+// Entries of dense B row `did` with columns below c (0 <= c <= B.cols).
+__device__ __forceinline__ int dense_rank(const DenseRows& dense, int did, long long c) {
+  const size_t g = (size_t)did * dense.stride + (size_t)(c >> 5);
+  const unsigned below = (1u << (c & 31)) - 1u;
+  return (int)(__ldg(dense.pre + g) + __popc(__ldg(dense.bits + g) & below));
+}
+
 // ORs the words of window [w0, w0 + span) of the listed dense B rows into bm (W words; thread
 // per word, plain read-modify-write: no other writer may run concurrently).
 template <int NT>
 __device__ __forceinline__ void or_dense_rows(unsigned* bm, int W, unsigned span, long long w0,
-                                              const DenseRows& dense, const int* dlist, int nd) {
+                                              const DenseRows& dense, const BlockChunk& ch,
+                                              const int* dlist, int nd) {
   const long long g0 = w0 >> 5;
   const int sh = (int)(w0 & 31);
   for (int w = threadIdx.x; w < W; w += NT) {
-    const long long g = g0 + w;
+    const long long g = g0 + w;   // g + 1 < stride: the window lies inside B's columns
     unsigned acc = 0u;
     for (int d = 0; d < nd; ++d) {
-      const unsigned* row = dense.bits + (size_t)dlist[d] * dense.words;
-      const unsigned x0 = __ldg(row + g);
-      const unsigned x1 = g + 1 < dense.words ? __ldg(row + g + 1) : 0u;
-      acc |= __funnelshift_r(x0, x1, sh);
+      const unsigned* row = dense.bits + (size_t)ch.be[dlist[d]] * dense.stride;
+      acc |= __funnelshift_r(__ldg(row + g), __ldg(row + g + 1), sh);
     }
     if (w == W - 1 && (span & 31u)) acc &= (1u << (span & 31u)) - 1u;
     bm[w] |= acc;

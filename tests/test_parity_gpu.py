@@ -220,6 +220,30 @@ def test_dense_b_rows_in_cta_symbolic_tier(op):
     assert st["tier_rows"]["block_rank"] > 0, st["tier_rows"]
 
 
+@pytest.mark.parametrize("op", ["ab", "ab_upper"])
+def test_dense_b_rows_in_window_tier(op):
+    """Dense rows of C (window tier) built mostly from B rows kept as bitmaps: their products
+    are added by per-warp column slices located through the bitmaps' popcount prefixes, the
+    rest with shared atomics."""
+    rng = np.random.default_rng(12)
+    k, cols = 256, (1 << 17) + 5000
+    brows = [np.unique(rng.integers(0, cols, cols // 7 if r % 32 == 5 else 200))
+             for r in range(k)]
+    brp = np.zeros(k + 1, np.int64)
+    brp[1:] = np.cumsum([len(r) for r in brows])
+    bci = np.concatenate(brows).astype(np.int32)
+    B = M.Csr(k, cols, brp.astype(np.int32), bci, rng.uniform(-1, 1, bci.size))
+    m = 100
+    arows = [np.unique(np.concatenate([rng.integers(0, k, 5), 32 * rng.integers(0, 8, 3) + 5]))
+             for _ in range(m)]
+    arp = np.zeros(m + 1, np.int64)
+    arp[1:] = np.cumsum([len(r) for r in arows])
+    aci = np.concatenate(arows).astype(np.int32)
+    A = M.Csr(m, k, arp.astype(np.int32), aci, rng.uniform(-1, 1, aci.size))
+    C, st = check(A, B, op=op)
+    assert st["tier_rows"]["window"] > 0, st["tier_rows"]
+
+
 @pytest.mark.parametrize("method", ["adaptive", "hash", "esc"])
 @pytest.mark.parametrize("name", ["uniform8", "stencil27", "banded", "random"])
 def test_sequential_tiers_are_bit_exact(name, method):
