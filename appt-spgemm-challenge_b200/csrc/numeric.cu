@@ -498,6 +498,7 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
   ch.bs = ch.piece_ex + NT;                                               // [NT]
   ch.be = ch.bs + NT;                                                     // [NT]
   int* dlist = ch.be + NT;                                                // [NT]
+  int* split = dlist + NT;                                                // [NT]
   __shared__ long long sbuf[NW + 1];
   __shared__ long long s_row;
   __shared__ int s_dcount;
@@ -515,17 +516,35 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
     const long long n = crp[i + 1] - c0;
     const int rs = A.rp[i], re = A.rp[i + 1];
     const bool multi = (long long)hi - lo + 1 > WC;
+    // window boundaries of every B row of the row, found once by one binary search per (entry,
+    // boundary) pair in parallel, when they fit the table (else every window searches)
+    const long long nwin = ((long long)hi - lo + WC) / WC;
+    const int T1 = (int)(nwin + 1 < NT ? nwin + 1 : NT);
+    const bool use_split = multi && (long long)(re - rs) * (nwin + 1) <= NT;
+    if (use_split) {
+      for (int x = tid; x < (re - rs) * T1; x += NT) {
+        const int e = x / T1, t = x - e * T1;
+        const int k = __ldg(A.ci + rs + e);
+        const int rb = __ldg(B.rp + k), rend = __ldg(B.rp + k + 1);
+        const long long c = (long long)lo + (long long)t * WC;
+        const bool skip = dense.id && __ldg(dense.id + k) >= 0;   // walked by bitmap
+        split[x] = skip ? 0 : c > hi ? rend : lower_bound_col(B.ci, rb, rend, (int)c);
+      }
+      __syncthreads();
+    }
     long long ob = 0;
     for (long long w0 = lo; w0 <= hi; w0 += WC) {
       const long long w1 = (w0 + WC < (long long)hi + 1) ? w0 + WC : (long long)hi + 1;
       const unsigned span = (unsigned)(w1 - w0);
       const int words = (int)((span + 31) >> 5);
+      const int wt = (int)((w0 - lo) / WC);
       for (int t = tid; t < (int)span; t += NT) acc[t] = 0.0;
       for (int w = tid; w < words; w += NT) bm[w] = 0u;
       for (int cb = rs; cb < re; cb += NT) {
         const int cn = (re - cb) < NT ? (re - cb) : NT;
         const int tp = load_block_chunk<NT>(A, B, cb, re, multi, w0, w1, ch, sbuf, dense.id,
-                                            dlist, &s_dcount);
+                                            dlist, &s_dcount, use_split ? split : nullptr, wt,
+                                            T1);
         for (int it = warp; it < tp; it += NW) {
           const int L = search_le(ch.piece_ex, cn, it);
           const int q0 = ch.bs[L] + (it - ch.piece_ex[L]) * kPiece;
@@ -754,7 +773,7 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
     }
     case kNumWindow: {
       constexpr int NT = 1024, WC = kWindowCols;
-      const size_t smem = (size_t)WC * 8 + (size_t)(WC / 32) * 4 + (size_t)NT * (8 + 12 + 4);
+      const size_t smem = (size_t)WC * 8 + (size_t)(WC / 32) * 4 + (size_t)NT * (8 + 12 + 8);
       auto kern = num_block_window_kernel<WC, NT>;
       static bool attr = false;
       if (!attr) {

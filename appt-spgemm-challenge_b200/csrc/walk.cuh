@@ -342,16 +342,19 @@ struct BlockChunk {   // one chunk of up to NT A entries of a row, in shared mem
   double* a;          // A value
 };
 
-// Loads A entries [cb, cb + NT) of the row (segments restricted to [w0, w1) when `multi`) and
-// returns the number of pieces. With `dense_id`, entries whose B row has a bitmap get no pieces:
-// their chunk indices are listed in dlist[0 .. *dcount), with bs = the B row's first entry and
-// be = its bitmap index. Contains barriers.
+// Loads A entries [cb, cb + NT) of the row (segments restricted to [w0, w1) when `multi`, by
+// binary search, or read from `split` -- split[e * split_stride + t] is the first entry of
+// window t in entry e's B row) and returns the number of pieces. With `dense_id`, entries whose
+// B row has a bitmap get no pieces: their chunk indices are listed in dlist[0 .. *dcount), with
+// bs = the B row's first entry and be = its bitmap index. Contains barriers.
 template <int NT>
 __device__ __forceinline__ int load_block_chunk(const Csr& A, const Csr& B, int cb, int re,
                                                 bool multi, long long w0, long long w1,
                                                 BlockChunk ch, long long* sbuf,
                                                 const int* dense_id = nullptr,
-                                                int* dlist = nullptr, int* dcount = nullptr) {
+                                                int* dlist = nullptr, int* dcount = nullptr,
+                                                const int* split = nullptr, int split_t = 0,
+                                                int split_stride = 0) {
   const int tid = threadIdx.x;
   const int p = cb + tid;
   int bs = 0, be = 0, did = -1;
@@ -364,7 +367,10 @@ __device__ __forceinline__ int load_block_chunk(const Csr& A, const Csr& B, int 
     a = __ldg(A.val + p);
     if (did < 0) {
       be = __ldg(B.rp + k + 1);
-      if (multi) {
+      if (multi && split) {
+        bs = split[tid * split_stride + split_t];
+        be = split[tid * split_stride + split_t + 1];
+      } else if (multi) {
         bs = lower_bound_col(B.ci, bs, be, (int)w0);
         be = lower_bound_col(B.ci, bs, be, (int)(w1 > 0x7fffffffll ? 0x7fffffff : w1));
       }
