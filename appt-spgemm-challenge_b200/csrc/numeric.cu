@@ -581,17 +581,43 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
                 ad = ch.a[t];
               }
               const int cnt = nd - d0 < 32 ? nd - d0 : 32;
+              const int w0i = (int)w0;   // columns of the slice lie in [w0, w1)
               for (int j = 0; j < cnt; ++j) {
                 const int q0 = __shfl_sync(0xffffffffu, s0, j);
                 const int q1 = __shfl_sync(0xffffffffu, s1, j);
                 const double a = __shfl_sync(0xffffffffu, ad, j);
-                for (int qb = q0; qb < q1; qb += 128) {
-                  PieceRound pr;
-                  load_piece_round<true>(B, qb + lane, q1, w0, pr);
+                const int* cp = B.ci + q0 + lane;
+                const double* vp = B.val + q0 + lane;
+                int q = q0;
+                for (; q + 128 <= q1; q += 128, cp += 128, vp += 128) {   // full rounds
+                  int c[4];
+                  double x[4];
+#pragma unroll
+                  for (int u = 0; u < 4; ++u) {
+                    c[u] = __ldg(cp + 32 * u);
+                    x[u] = __ldg(vp + 32 * u);
+                  }
+#pragma unroll
+                  for (int u = 0; u < 4; ++u) {
+                    double* p = acc + (c[u] - w0i);
+                    *p = fma(a, x[u], *p);
+                  }
+                }
+                if (q < q1) {   // last partial round
+                  int c[4];
+                  double x[4];
+#pragma unroll
+                  for (int u = 0; u < 4; ++u) {
+                    const bool v = q + lane + 32 * u < q1;
+                    c[u] = v ? __ldg(cp + 32 * u) : -1;
+                    x[u] = v ? __ldg(vp + 32 * u) : 0.0;
+                  }
 #pragma unroll
                   for (int u = 0; u < 4; ++u)
-                    if (pr.off[u] < span)
-                      acc[pr.off[u]] = __dadd_rn(acc[pr.off[u]], __dmul_rn(a, pr.x[u]));
+                    if (c[u] >= 0) {
+                      double* p = acc + (c[u] - w0i);
+                      *p = fma(a, x[u], *p);
+                    }
                 }
                 __syncwarp();   // the next row's entries may hit these columns in other lanes
               }
