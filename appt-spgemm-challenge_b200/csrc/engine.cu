@@ -71,8 +71,40 @@ struct DeviceCtx {
   // on a device are serialised by `mu` and each ends with its work complete
   unsigned* harena = nullptr;
   bool harena_tried = false;
+  // side streams: the per-bin kernels of one phase run concurrently (the small bins' kernels and
+  // the tails of the large ones overlap instead of queueing behind each other)
+  static constexpr int kSide = 3;
+  cudaStream_t side[kSide] = {};
+  cudaEvent_t ev_fork = nullptr;
+  cudaEvent_t ev_join[kSide] = {};
   std::mutex mu;
   bool ok = false;
+};
+
+// Fans the launches of one phase out over `s` and the context's side streams: fork() makes the
+// side streams wait for the work queued on `s` so far, at(j) is the stream of launch j, join()
+// makes `s` wait for everything launched on the side streams.
+struct Fan {
+  DeviceCtx* ctx;
+  cudaStream_t s;
+  cudaError_t fork() {
+    cudaError_t e = cudaEventRecord(ctx->ev_fork, s);
+    for (int j = 0; j < DeviceCtx::kSide && e == cudaSuccess; ++j)
+      e = cudaStreamWaitEvent(ctx->side[j], ctx->ev_fork, 0);
+    return e;
+  }
+  cudaStream_t at(int j) const {
+    const int l = j % (DeviceCtx::kSide + 1);
+    return l == 0 ? s : ctx->side[l - 1];
+  }
+  cudaError_t join() {
+    cudaError_t e = cudaSuccess;
+    for (int j = 0; j < DeviceCtx::kSide && e == cudaSuccess; ++j) {
+      e = cudaEventRecord(ctx->ev_join[j], ctx->side[j]);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ctx->ev_join[j], 0);
+    }
+    return e;
+  }
 };
 
 static DeviceCtx g_ctx[64];
@@ -99,6 +131,11 @@ static int get_ctx(int device, DeviceCtx** out) {
     CK(cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, device));
     CK(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&c.copy_stream, cudaStreamNonBlocking));
+    for (int j = 0; j < DeviceCtx::kSide; ++j) {
+      CK(cudaStreamCreateWithFlags(&c.side[j], cudaStreamNonBlocking));
+      CK(cudaEventCreateWithFlags(&c.ev_join[j], cudaEventDisableTiming));
+    }
+    CK(cudaEventCreateWithFlags(&c.ev_fork, cudaEventDisableTiming));
     cudaMemPoolProps props;
     std::memset(&props, 0, sizeof(props));
     props.allocType = cudaMemAllocationTypePinned;
@@ -345,7 +382,7 @@ constexpr long long kSmallNnz = 1 << 21;
 
 static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
                         cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C, CallStats* st,
-                        bool* fallback) {
+                        bool* fallback, cudaEvent_t vals_ready) {
   *fallback = false;
   const int m = A.rows;
   const int sms = ctx->num_sms;
@@ -399,6 +436,7 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
     return kErrOom;
   }
   tm.begin(kPhNumeric);
+  if (vals_ready) CK(cudaStreamWaitEvent(s, vals_ready, 0));
   launch_numeric_rank_all(boff, m, gidx, A, B, lo, hi, crp, cci, cval, err, sms, s);
   note_launches(1);
   tm.end();
@@ -427,15 +465,21 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   return kOk;
 }
 
+// vals_ready (may be null): event after which A's and B's values are in place; kernels that
+// read values wait for it.
 static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long long b_nnz,
                            int upper, int row_base, int method, cudaStream_t s, Scratch& sc,
-                           PhaseTimer& tm, DevC* C, CallStats* st, HostSink* sink) {
-  if (method == kMethodEsc)
+                           PhaseTimer& tm, DevC* C, CallStats* st, HostSink* sink,
+                           cudaEvent_t vals_ready = nullptr) {
+  if (method == kMethodEsc) {
+    if (vals_ready) CK(cudaStreamWaitEvent(s, vals_ready, 0));
     return esc_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st);
+  }
   if (method == kMethodAdaptive && A.rows > 0 && A.rows <= kSmallRows && a_nnz <= kSmallNnz &&
       !env_flag("APPT_NO_SMALL_PATH")) {
     bool fallback = false;
-    const int rc = small_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st, &fallback);
+    const int rc = small_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st, &fallback,
+                                vals_ready);
     if (rc != kOk || !fallback) return rc;
   }
   const int m = A.rows;
@@ -524,9 +568,12 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
     }
   }
   if (m > 0) {
+    Fan fan{ctx, s};
+    CK(fan.fork());
     for (int b = 0; b < kNumSymBins; ++b)
       launch_symbolic(b, rows_sym, boff_sym, A, B, upper, row_base, lo, hi, flop, row_nnz, handoff,
-                      dense, err + 3, err, sms, s);
+                      dense, err + 3, err, sms, fan.at(b));
+    CK(fan.join());
     note_launches(kNumSymBins);
     if (method == kMethodMerge) {
       launch_merge_count(rows_sym, boff_sym, kSymMergeBin, A, B, upper, row_base, row_nnz, err,
@@ -633,7 +680,11 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
   }
 
   tm.begin(kPhNumeric);
+  if (vals_ready) CK(cudaStreamWaitEvent(s, vals_ready, 0));
   for (int k = 0; k < K; ++k) {
+    Fan fan{ctx, s};
+    CK(fan.fork());
+    int nl = 0;
     for (int b = 0; b < kNumNumBins; ++b) {
       const long long nr_all = boff[b + 1] - boff[b];
       if (nr_all <= 0) continue;
@@ -641,14 +692,16 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
       const long long* bo = K > 1 ? bsub + (size_t)b * K + k : boff_num;
       const long long nr = K > 1 ? nr_all / K + 1 : nr_all;   // grid sizing only
       int* ctr = nctr + (size_t)k * kNumNumBins + b;
+      const cudaStream_t bs = fan.at(nl++);
       if (b == kNumMerge)
         launch_merge_numeric(rows_num, bo, b, nr, A, B, upper, row_base, crp, cci, cval, err, sms,
-                             s);
+                             bs);
       else
         launch_numeric(b, rows_num, bo, nr, A, B, upper, row_base, lo, hi, flop, handoff, dense,
-                       crp, cci, cval, ctr, err, sms, s);
+                       crp, cci, cval, ctr, err, sms, bs);
       note_launches(1);
     }
+    CK(fan.join());
     if (sink) {
       const long long e0 = cstart[k], e1 = cstart[k + 1];
       CK(cudaEventRecord(evs[k], s));
@@ -692,7 +745,12 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
 }
 
 // ------------------------------------------------------------------ operand staging
-static int stage_operand(const MatView& M, Scratch& sc, cudaStream_t s, Csr* out) {
+// Copies a host operand into pool memory on `s`; with `vs` the values go on that stream instead
+// (after an event that orders them behind the allocation on `s`), so that the index-only phases
+// (analyze, symbolic) overlap their copy -- the caller must make `s` wait for `vs` before any
+// kernel reads the values.
+static int stage_operand(const MatView& M, Scratch& sc, cudaStream_t s, Csr* out,
+                         cudaStream_t vs = nullptr) {
   int* rp = sc.get<int>((size_t)M.rows + 1);
   int* ci = sc.get<int>((size_t)M.nnz);
   double* val = sc.get<double>((size_t)M.nnz);
@@ -713,8 +771,15 @@ static int stage_operand(const MatView& M, Scratch& sc, cudaStream_t s, Csr* out
   }
   if (M.nnz > 0) {
     CK(cudaMemcpyAsync(ci, M.ci + rp0, sizeof(int) * (size_t)M.nnz, cudaMemcpyHostToDevice, s));
+    if (vs) {
+      cudaEvent_t alloc_done;
+      CK(cudaEventCreateWithFlags(&alloc_done, cudaEventDisableTiming));
+      CK(cudaEventRecord(alloc_done, s));
+      CK(cudaStreamWaitEvent(vs, alloc_done, 0));
+      cudaEventDestroy(alloc_done);
+    }
     CK(cudaMemcpyAsync(val, M.val + rp0, sizeof(double) * (size_t)M.nnz, cudaMemcpyHostToDevice,
-                       s));
+                       vs ? vs : s));
   }
   out->rp = rp;
   out->ci = ci;
@@ -789,8 +854,25 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
   }
   Csr dA{}, dB{};
   tm.begin(kPhH2D);
+  // host operands of the binned pipeline: values copied on the copy stream while the index-only
+  // phases run; `vals` orders them before the numeric phase (and before anything is freed)
+  struct ValuesReady {
+    cudaStream_t s = nullptr;
+    cudaEvent_t ev = nullptr;
+    void wait() {   // make `s` wait for the values; idempotent
+      if (ev) {
+        cudaStreamWaitEvent(s, ev, 0);
+        cudaEventSynchronize(ev);   // host buffers stay untouched once this returns
+        cudaEventDestroy(ev);
+        ev = nullptr;
+      }
+    }
+    ~ValuesReady() { wait(); }
+  } vals;
+  const bool defer = opt.in_mem == 0 && ab && opt.method != kMethodEsc;
+  cudaStream_t vs = defer ? ctx->copy_stream : nullptr;
   if (opt.in_mem == 0) {
-    rc = stage_operand(A, sc, s, &dA);
+    rc = stage_operand(A, sc, s, &dA, vs);
     if (rc) return rc;
   } else {
     dA = Csr{A.rp, A.ci, A.val, (int)A.rows, (int)A.cols};
@@ -804,7 +886,7 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
       }
       b_nnz = B->nnz;
       if (opt.in_mem == 0) {
-        rc = stage_operand(*B, sc, s, &dB);
+        rc = stage_operand(*B, sc, s, &dB, vs);
         if (rc) return rc;
       } else {
         dB = Csr{B->rp, B->ci, B->val, (int)B->rows, (int)B->cols};
@@ -827,8 +909,13 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
     return kErrInvalid;
   }
   const int upper = (opt.op == kOpAATUpper || opt.op == kOpABUpper) ? 1 : 0;
+  if (defer) {
+    vals.s = s;
+    CK(cudaEventCreateWithFlags(&vals.ev, cudaEventDisableTiming));
+    CK(cudaEventRecord(vals.ev, vs));
+  }
   return multiply_device(ctx, dA, dB, A.nnz, b_nnz, upper, (int)opt.row_base, opt.method, s, sc,
-                         tm, dc, st, sink);
+                         tm, dc, st, sink, vals.ev);
 }
 
 // Pinned host blocks for results returned in host memory: a block released by free_out is kept
