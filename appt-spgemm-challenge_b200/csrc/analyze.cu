@@ -34,7 +34,54 @@ __device__ __forceinline__ int sym_bin_of(long long flop, long long span, long l
   return kSymBlock;
 }
 
-// LPR lanes cooperate on one row; 32/LPR rows per warp per step.
+// Outputs of one analysed row: products count, span, symbolic bin (255: nothing to compute).
+__device__ __forceinline__ void finish_row(long long row, int upper, int row_base, int method,
+                                           long long f, int lo, int hi, int bad, int rowlen,
+                                           long long* flop, int* lo_out, int* hi_out,
+                                           uint8_t* symkey, int* row_nnz, int* err,
+                                           long long* span_out) {
+  const int ig = (int)row + row_base;
+  if (upper && lo < ig) lo = ig;
+  const long long span = (hi >= lo) ? (long long)hi - lo + 1 : 0;
+  flop[row] = f;
+  lo_out[row] = lo;
+  hi_out[row] = hi;
+  int key;
+  if (bad) {
+    key = 255;
+    set_error(err, kErrBounds);
+  } else if (method == kMethodMerge && rowlen <= kMergeMaxLists) {
+    key = (f > 0 && span > 0) ? kNumSymBins : 255;   // the merge-count bin
+  } else {
+    key = sym_bin_of(f, span, rowlen);
+  }
+  symkey[row] = (uint8_t)key;
+  if (key == 255) row_nnz[row] = 0;
+  *span_out = span;
+}
+
+// Products count and span contributions of entries [p0, re) of a row, every `step`-th entry.
+__device__ __forceinline__ void scan_entries(const Csr& A, const Csr& B, int p0, int re, int step,
+                                             long long& f, int& lo, int& hi, int& bad) {
+#pragma unroll 4
+  for (int p = p0; p < re; p += step) {
+    const int k = A.ci[p];
+    if ((unsigned)k >= (unsigned)B.rows) {   // column outside B: flag, never dereference
+      bad = 1;
+      continue;
+    }
+    const int b0 = B.rp[k], b1 = B.rp[k + 1];
+    if (b1 > b0) {
+      f += b1 - b0;
+      lo = min(lo, B.ci[b0]);
+      hi = max(hi, B.ci[b1 - 1]);
+    }
+  }
+}
+
+// LPR lanes cooperate on one row; 32/LPR rows per warp per step. Rows longer than 32 * LPR
+// entries are left to analyze_long_kernel (a CTA per row), so that one long row does not hold
+// its warp for thousands of dependent steps.
 template <int LPR>
 __global__ void __launch_bounds__(kAnThreads) analyze_kernel(Csr A, Csr B, int upper, int row_base,
                                                              int method, long long* flop, int* lo_out,
@@ -50,27 +97,18 @@ __global__ void __launch_bounds__(kAnThreads) analyze_kernel(Csr A, Csr B, int u
   unsigned long long my_flop_sum = 0, my_flop_max = 0, my_span_max = 0;
   for (long long base = gw * RPW; base < m; base += warps_total * RPW) {
     const long long row = base + grp;
-    const bool valid = row < m;
     long long f = 0;
     int lo = INT_MAX, hi = -1;
     int bad = 0;
     int rowlen = 0;
+    bool valid = row < m;
     if (valid) {
       const int rs = A.rp[row], re = A.rp[row + 1];
       rowlen = re - rs;
-      for (int p = rs + sub; p < re; p += LPR) {
-        const int k = A.ci[p];
-        if ((unsigned)k >= (unsigned)B.rows) {   // column outside B: flag, never dereference
-          bad = 1;
-          continue;
-        }
-        const int b0 = B.rp[k], b1 = B.rp[k + 1];
-        if (b1 > b0) {
-          f += b1 - b0;
-          lo = min(lo, B.ci[b0]);
-          hi = max(hi, B.ci[b1 - 1]);
-        }
-      }
+      if (rowlen > 32 * LPR)
+        valid = false;   // a long row
+      else
+        scan_entries(A, B, rs + sub, re, LPR, f, lo, hi, bad);
     }
 #pragma unroll
     for (int o = 1; o < LPR; o <<= 1) {
@@ -80,23 +118,9 @@ __global__ void __launch_bounds__(kAnThreads) analyze_kernel(Csr A, Csr B, int u
       hi = max(hi, __shfl_xor_sync(kFull, hi, o));
     }
     if (valid && sub == 0) {
-      const int ig = (int)row + row_base;
-      if (upper && lo < ig) lo = ig;
-      const long long span = (hi >= lo) ? (long long)hi - lo + 1 : 0;
-      flop[row] = f;
-      lo_out[row] = lo;
-      hi_out[row] = hi;
-      int key;
-      if (bad) {
-        key = 255;
-        set_error(err, kErrBounds);
-      } else if (method == kMethodMerge && rowlen <= kMergeMaxLists) {
-        key = (f > 0 && span > 0) ? kNumSymBins : 255;   // the merge-count bin
-      } else {
-        key = sym_bin_of(f, span, rowlen);
-      }
-      symkey[row] = (uint8_t)key;
-      if (key == 255) row_nnz[row] = 0;
+      long long span;
+      finish_row(row, upper, row_base, method, f, lo, hi, bad, rowlen, flop, lo_out, hi_out,
+                 symkey, row_nnz, err, &span);
       my_flop_sum += (unsigned long long)f;
       my_flop_max = max(my_flop_max, (unsigned long long)f);
       my_span_max = max(my_span_max, (unsigned long long)span);
@@ -126,6 +150,64 @@ __global__ void __launch_bounds__(kAnThreads) analyze_kernel(Csr A, Csr B, int u
     if (s) atomicAdd(&stats->total_flop, s);
     if (mf) atomicMax(&stats->max_flop, mf);
     if (ms) atomicMax(&stats->max_span, ms);
+  }
+}
+
+// The rows analyze_kernel<LPR> leaves (more than `min_len` entries): each CTA checks a chunk of
+// kAnThreads rows, lists its long ones in shared memory and walks each with all its threads.
+__global__ void __launch_bounds__(kAnThreads) analyze_long_kernel(
+    Csr A, Csr B, int upper, int row_base, int method, int min_len, long long* flop,
+    int* lo_out, int* hi_out, uint8_t* symkey, int* row_nnz, AnalyzeStats* stats, int* err) {
+  __shared__ int s_list[kAnThreads];
+  __shared__ int s_n;
+  __shared__ long long s_f[kAnThreads / 32];
+  __shared__ int s_lo[kAnThreads / 32], s_hi[kAnThreads / 32], s_bad[kAnThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int m = A.rows;
+  for (long long c0 = (long long)blockIdx.x * kAnThreads; c0 < m;
+       c0 += (long long)gridDim.x * kAnThreads) {
+    if (tid == 0) s_n = 0;
+    __syncthreads();
+    const long long row = c0 + tid;
+    if (row < m && A.rp[row + 1] - A.rp[row] > min_len) s_list[atomicAdd(&s_n, 1)] = (int)row;
+    __syncthreads();
+    const int n = s_n;
+    for (int t = 0; t < n; ++t) {
+      const int r = s_list[t];
+      const int rs = A.rp[r], re = A.rp[r + 1];
+      long long f = 0;
+      int lo = INT_MAX, hi = -1, bad = 0;
+      scan_entries(A, B, rs + tid, re, kAnThreads, f, lo, hi, bad);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        f += __shfl_xor_sync(kFull, f, o);
+        bad |= __shfl_xor_sync(kFull, bad, o);
+        lo = min(lo, __shfl_xor_sync(kFull, lo, o));
+        hi = max(hi, __shfl_xor_sync(kFull, hi, o));
+      }
+      if (lane == 0) {
+        s_f[warp] = f;
+        s_lo[warp] = lo;
+        s_hi[warp] = hi;
+        s_bad[warp] = bad;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        for (int w = 1; w < kAnThreads / 32; ++w) {
+          f += s_f[w];
+          lo = min(lo, s_lo[w]);
+          hi = max(hi, s_hi[w]);
+          bad |= s_bad[w];
+        }
+        long long span;
+        finish_row(r, upper, row_base, method, f, lo, hi, bad, re - rs, flop, lo_out, hi_out,
+                   symkey, row_nnz, err, &span);
+        if (f) atomicAdd(&stats->total_flop, (unsigned long long)f);
+        atomicMax(&stats->max_flop, (unsigned long long)f);
+        atomicMax(&stats->max_span, (unsigned long long)span);
+      }
+      __syncthreads();
+    }
   }
 }
 
@@ -178,6 +260,12 @@ void launch_analyze(Csr A, Csr B, int upper, int row_base, int method, int lanes
   long long blocks = (m + rows_per_block - 1) / rows_per_block;
   long long cap = (long long)num_sms * 16;
   if (blocks > cap) blocks = cap;
+  // rows beyond 32 * lpr entries: a CTA each
+  long long lblocks = (m + kAnThreads - 1) / kAnThreads;
+  if (lblocks > (long long)num_sms * 8) lblocks = (long long)num_sms * 8;
+  analyze_long_kernel<<<(unsigned)lblocks, kAnThreads, 0, s>>>(A, B, upper, row_base, method,
+                                                               32 * lpr, flop, lo, hi, symkey,
+                                                               row_nnz, stats, err);
   switch (lpr) {
     case 4:
       analyze_kernel<4><<<(unsigned)blocks, kAnThreads, 0, s>>>(A, B, upper, row_base, method, flop,

@@ -281,11 +281,7 @@ struct DevC {            // device-resident result, allocations owned by the poo
 };
 
 static int lanes_per_row(long long nnz, long long rows) {
-  const double avg = rows > 0 ? (double)nnz / (double)rows : 0.0;
-  if (avg <= 6) return 4;
-  if (avg <= 12) return 8;
-  if (avg <= 24) return 16;
-  return 32;
+  return analyze_lanes_per_row(nnz, rows);
 }
 
 static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
@@ -311,7 +307,7 @@ static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, 
   tm.begin(kPhAnalyze);
   launch_analyze(A, B, upper, row_base, kMethodEsc, lanes_per_row(a_nnz, m), flop, lo, hi, key,
                  row_nnz, gst, err, sms, s);
-  note_launches(m > 0 ? 1 : 0);
+  note_launches(m > 0 ? 2 : 0);
   note_launches(scan_exclusive(flop, foff, m, scs, s));
   CK(cudaMemcpyAsync(ctx->stage, foff + m, 8, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(ctx->stage + 64, gst, sizeof(AnalyzeStats), cudaMemcpyDeviceToHost, s));
@@ -538,7 +534,7 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
   tm.begin(kPhAnalyze);
   launch_analyze(A, B, upper, row_base, method, lanes_per_row(a_nnz, m), flop, lo, hi, symkey,
                  row_nnz, gst, err, sms, s);
-  note_launches(m > 0 ? 1 : 0);   // analyze
+  note_launches(m > 0 ? 2 : 0);   // analyze (short rows, long rows)
   note_launches(partition_rows(symkey, m, nsb, rows_sym, boff_sym, pscr, s));
 
   tm.begin(kPhSymbolic);
@@ -1332,7 +1328,7 @@ int row_products(const MatView& A, const MatView* B, const CallOptions& opt, lon
   CK(cudaMemsetAsync(gst, 0, sizeof(AnalyzeStats), s));
   launch_analyze(dA, dB, 0, 0, kMethodAdaptive, lanes_per_row(A.nnz, A.rows), flop, lo, hi, key,
                  rn, gst, nullptr, ctx->num_sms, s);
-  note_launches(m > 0 ? 1 : 0);
+  note_launches(m > 0 ? 2 : 0);
   if (m > 0) CK(cudaMemcpyAsync(out, flop, sizeof(long long) * (size_t)m, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
   return kOk;

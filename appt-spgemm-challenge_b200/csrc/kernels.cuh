@@ -134,6 +134,15 @@ void block_bin_bounds(const int* rows, const long long* bin_off, int nb, long lo
 void iota(int* out, int n, cudaStream_t s);
 
 // analyze.cu
+// Lanes per row of the analysis of short rows (rows beyond 32 x that many entries take a CTA).
+inline int analyze_lanes_per_row(long long nnz, long long rows) {
+  const double avg = rows > 0 ? (double)nnz / (double)rows : 0.0;
+  if (avg <= 32) return 4;
+  if (avg <= 64) return 8;
+  if (avg <= 128) return 16;
+  return 32;
+}
+// Launches two kernels (short rows by lane groups, long rows by CTAs).
 void launch_analyze(Csr A, Csr B, int upper, int row_base, int method, int lanes_per_row,
                     long long* flop, int* lo, int* hi, uint8_t* symkey, int* row_nnz,
                     AnalyzeStats* stats, int* err, int num_sms, cudaStream_t s);

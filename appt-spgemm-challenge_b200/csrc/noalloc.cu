@@ -162,11 +162,10 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
   // the previous call's contents stay in the array: clear what must start at zero
   cudaMemsetAsync(gst, 0, sizeof(AnalyzeStats), s);
   cudaMemsetAsync(err, 0, (4 + kMaxBins) * sizeof(int), s);
-  const double avg = m > 0 ? (double)A.nnz / (double)m : 0.0;
-  const int lpr = avg <= 6 ? 4 : avg <= 12 ? 8 : avg <= 24 ? 16 : 32;
+  const int lpr = analyze_lanes_per_row(A.nnz, m);
   launch_analyze(dA, dB, 0, 0, kMethodAdaptive, lpr, flop, lo, hi, symkey, row_nnz, gst, err, sms,
                  s);
-  long long launched = m > 0 ? 2 : 0;   // analyze, classify
+  long long launched = m > 0 ? 3 : 0;   // analyze (two kernels), classify
   launched += partition_rows(symkey, m, kNumSymBins + 1, rows_sym, boff_sym, pscr, s);
   if (m > 0)
     for (int b = 0; b < kNumSymBins; ++b)
