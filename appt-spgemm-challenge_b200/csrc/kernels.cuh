@@ -10,7 +10,9 @@ namespace appt {
 constexpr int kMaxBins = 32;
 
 // Capacities shared by the classifier and the kernels.
-constexpr int kWindowCols = 16384;      // CTA window tier: columns per window
+constexpr int kWindowCols = 16384;      // CTA window tier: window scale of the classifier's cost
+                                        // model (the kernel itself walks 8192-column windows)
+constexpr int kWindowSplit = 1536;      // CTA window tier: per-row table of B-row window bounds
 constexpr int kHashBlockSlots = 8192;   // CTA hash tier: table slots (rows with nnz <= slots/2)
 constexpr int kSymBlockWords = 32768;   // CTA symbolic bitmap window: 2^20 columns
 constexpr int kMergeMaxLists = 256;     // merge tier: rows with more A entries use other tiers

@@ -11,7 +11,7 @@
 //           column its output position, values accumulate there directly (no table, no sort)
 //   hash    warp per row; table of T slots (int key + fp64 value), compaction, warp bitonic sort
 //   hashB   CTA per row; 8192-slot table, block bitonic sort
-//   window  CTA per row; dense windows of 16384 columns walked over the row's span (heavy rows)
+//   window  CTA per row; dense windows of 8192 columns walked over the row's span (heavy rows)
 // The warp tiers visit products k-sequentially (walk.cuh) and round like the sequential
 // algorithm (no FMA), so their sums are bit-identical to the CPU oracle's; the CTA tiers
 // accumulate with shared-memory atomics (order-dependent rounding, within the tolerance).
@@ -480,13 +480,14 @@ __global__ void __launch_bounds__(NT) num_block_hash_kernel(
 // window's entries are emitted in column order at positions from one block scan of the bitmap
 // words' popcounts.
 template <int WC, int NT>
-__global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
+__global__ void __launch_bounds__(NT, 1024 / NT) num_block_window_kernel(
     const int* rows, const long long* bin_off, int bin, Csr A, Csr B, const int* lo_arr,
     const int* hi_arr, DenseRows dense, const long long* crp, int* cci, double* cval,
     int* row_counter, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
   constexpr int NW = NT / 32;
   constexpr int WW = WC / 32;
+  constexpr int kSplit = kWindowSplit;      // (entry, window boundary) table entries
   constexpr int WPW = (WW + NW - 1) / NW;   // bitmap words per warp in the emit
   constexpr int SUB = WC / NW;              // columns per warp in the dense-row products
   static_assert(WPW <= 32, "one bitmap word per lane when counting a warp's words");
@@ -498,7 +499,7 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
   ch.bs = ch.piece_ex + NT;                                               // [NT]
   ch.be = ch.bs + NT;                                                     // [NT]
   int* dlist = ch.be + NT;                                                // [NT]
-  int* split = dlist + NT;                                                // [NT]
+  int* split = dlist + NT;                                                // [kSplit]
   __shared__ long long sbuf[NW + 1];
   __shared__ long long s_row;
   __shared__ int s_dcount;
@@ -519,8 +520,9 @@ __global__ void __launch_bounds__(NT, 1) num_block_window_kernel(
     // window boundaries of every B row of the row, found once by one binary search per (entry,
     // boundary) pair in parallel, when they fit the table (else every window searches)
     const long long nwin = ((long long)hi - lo + WC) / WC;
-    const int T1 = (int)(nwin + 1 < NT ? nwin + 1 : NT);
-    const bool use_split = multi && (long long)(re - rs) * (nwin + 1) <= NT;
+    const int T1 = (int)(nwin + 1 < kSplit ? nwin + 1 : kSplit);
+    const bool use_split =   // one chunk of A entries (the table is indexed by chunk position)
+        multi && re - rs <= NT && (long long)(re - rs) * (nwin + 1) <= kSplit;
     if (use_split) {
       for (int x = tid; x < (re - rs) * T1; x += NT) {
         const int e = x / T1, t = x - e * T1;
@@ -798,15 +800,17 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
       break;
     }
     case kNumWindow: {
-      constexpr int NT = 1024, WC = kWindowCols;
-      const size_t smem = (size_t)WC * 8 + (size_t)(WC / 32) * 4 + (size_t)NT * (8 + 12 + 8);
+      // two CTAs per SM: one's barriers and L2 waits overlap the other's work
+      constexpr int NT = 512, WC = 8192;
+      const size_t smem = (size_t)WC * 8 + (size_t)(WC / 32) * 4 + (size_t)NT * (8 + 12 + 4) +
+                          (size_t)kWindowSplit * 4;
       auto kern = num_block_window_kernel<WC, NT>;
       static bool attr = false;
       if (!attr) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = true;
       }
-      const long long grid = nrows < num_sms ? nrows : num_sms;
+      const long long grid = nrows < 2 * num_sms ? nrows : 2 * num_sms;
       kern<<<(unsigned)grid, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, dense, crp, cci,
                                             cval, row_counter, err);
       break;
