@@ -53,6 +53,14 @@ def exchange_nnz(dist, my_nnz: int, device) -> np.ndarray:
     return block_offsets(torch.cat(parts).cpu().numpy())
 
 
+def exchange_nnz_into(dist, my_nnz: int, out) -> None:
+    """The same all-gather into a preallocated int64 tensor of world_size entries, without
+    waiting for it on the host (block_offsets(out.cpu().numpy()) gives the offsets later)."""
+    import torch
+    mine = torch.full((1,), int(my_nnz), dtype=torch.int64, device=out.device)
+    dist.all_gather_into_tensor(out, mine)
+
+
 def replicate(dist, tensors, src: int = 0) -> None:
     """Broadcast operand arrays (already allocated with the right sizes on every rank)."""
     for t in tensors:

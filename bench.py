@@ -452,9 +452,11 @@ def main():
             num_ms += res.stats["ms_phase"]["numeric"]
             st = res.stats
             res.free()
-        if world > 1:
-            D.exchange_nnz(dist, nnz_tot, dev)
+        if world > 1:   # global row offsets of C: one all-gather, read on the host later
+            D.exchange_nnz_into(dist, nnz_tot, nnz_all)
         return nnz_tot, num_ms, st
+
+    nnz_all = torch.zeros(world, dtype=torch.int64, device=dev)
 
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     for _ in range(args.warmup):
@@ -494,6 +496,9 @@ def main():
         pr = torch.tensor([my_products, c_nnz], dtype=torch.int64, device=dev)
         dist.all_reduce(pr)
         all_products, all_cnnz = int(pr[0]), int(pr[1])
+        offs = D.block_offsets(nnz_all.cpu().numpy())   # the step's exchange, read once here
+        if int(offs[-1]) != all_cnnz:
+            raise RuntimeError(f"nnz exchange gave {int(offs[-1])} entries, ranks hold {all_cnnz}")
     else:
         t_total_max = t_total
         all_products, all_cnnz = my_products, c_nnz
