@@ -220,6 +220,23 @@ def test_dense_b_rows_in_cta_symbolic_tier(op):
     assert st["tier_rows"]["block_rank"] > 0, st["tier_rows"]
 
 
+@pytest.mark.parametrize("cols", [1 << 22, 1 << 25])
+@pytest.mark.parametrize("op", ["ab", "ab_upper"])
+def test_cta_hash_tier_wide_spans(op, cols):
+    """Rows of C with 513..2048 entries spread over millions of columns take the CTA hash tier
+    (hash table sized from the exact nnz, compaction and an in-table sort)."""
+    rng = np.random.default_rng(13)
+    k = 64
+    brows = [np.unique(rng.integers(0, cols, 100)) for _ in range(k)]
+    brp = np.zeros(k + 1, np.int64)
+    brp[1:] = np.cumsum([len(r) for r in brows])
+    bci = np.concatenate(brows).astype(np.int32)
+    B = M.Csr(k, cols, brp.astype(np.int32), bci, rng.uniform(-1, 1, bci.size))
+    A = M.random_csr(200, k, 0.15, 6)
+    C, st = check(A, B, op=op)
+    assert st["tier_rows"]["hash_block"] > 0, st["tier_rows"]
+
+
 @pytest.mark.parametrize("op", ["ab", "ab_upper"])
 def test_dense_b_rows_in_window_tier(op):
     """Dense rows of C (window tier) built mostly from B rows kept as bitmaps: their products
