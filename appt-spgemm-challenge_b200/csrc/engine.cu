@@ -154,6 +154,20 @@ static int get_ctx(int device, DeviceCtx** out) {
   return kOk;
 }
 
+// Lays several arrays out in one allocation (256-byte aligned): a first pass with base == nullptr
+// only adds up the bytes, a second pass over a block of that size hands out the pointers.
+struct Carver {
+  char* base = nullptr;
+  size_t off = 0;
+  template <typename T>
+  T* take(size_t count) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += (count ? count : 1) * sizeof(T);
+    return p;
+  }
+};
+
 // Stream-ordered scratch allocations freed when the object goes out of scope, unless detached.
 struct Scratch {
   DeviceCtx* ctx;
@@ -162,12 +176,24 @@ struct Scratch {
   std::vector<std::vector<int>> host_keep;   // host staging copies alive until the call ends
   bool failed = false;
   Scratch(DeviceCtx* c, cudaStream_t st) : ctx(c), s(st) {}
+  // One allocation for the arrays `layout(Carver&)` takes (called twice: sizes, then pointers).
+  template <typename F>
+  bool carve(F&& layout) {
+    Carver sizes;
+    layout(sizes);
+    char* base = get<char>(sizes.off, true);   // per-call arrays: never beside C in the big pool
+    if (!base) return false;
+    Carver c;
+    c.base = base;
+    layout(c);
+    return true;
+  }
   template <typename T>
-  T* get(size_t count) {
+  T* get(size_t count, bool small_pool = false) {
     size_t bytes = count * sizeof(T);
     if (bytes == 0) bytes = 256;
     void* p = nullptr;
-    cudaMemPool_t pool = bytes >= (size_t(64) << 20) ? ctx->pool_big : ctx->pool;
+    cudaMemPool_t pool = !small_pool && bytes >= (size_t(64) << 20) ? ctx->pool_big : ctx->pool;
     if (cudaMallocFromPoolAsync(&p, bytes, pool, s) != cudaSuccess) {
       cudaGetLastError();
       failed = true;
@@ -382,20 +408,24 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   *fallback = false;
   const int m = A.rows;
   const int sms = ctx->num_sms;
-  int* lo = sc.get<int>(m);
-  int* hi = sc.get<int>(m);
-  int* row_nnz = sc.get<int>(m);
-  long long* crp = sc.get<long long>((size_t)m + 1);
-  long long* boff = sc.get<long long>(2);
-  unsigned long long* tflop = sc.get<unsigned long long>(1);
-  int* err = sc.get<int>(4);
-  long long* scs = sc.get<long long>(scan_scratch_elems(m));
+  int *lo, *hi, *row_nnz, *err;
+  long long *boff, *scs;
+  unsigned long long* tflop;
+  sc.carve([&](Carver& c) {   // err and tflop first: one memset clears both
+    err = c.take<int>(4);
+    tflop = c.take<unsigned long long>(1);
+    lo = c.take<int>(m);
+    hi = c.take<int>(m);
+    row_nnz = c.take<int>(m);
+    boff = c.take<long long>(2);
+    scs = c.take<long long>(scan_scratch_elems(m));
+  });
+  long long* crp = sc.get<long long>((size_t)m + 1);   // handed to the caller with C
   if (sc.failed) {
     set_error("device pool allocation failed");
     return kErrOom;
   }
-  CK(cudaMemsetAsync(err, 0, sizeof(int) * 4, s));
-  CK(cudaMemsetAsync(tflop, 0, sizeof(unsigned long long), s));
+  CK(cudaMemsetAsync(err, 0, (char*)(tflop + 1) - (char*)err, s));
   const int gidx = group_index(a_nnz, m);   // B rows' average length taken from A's
   tm.begin(kPhSymbolic);
   launch_symbolic_small(A, B, upper, row_base, gidx, lo, hi, row_nnz, boff, tflop, err, sms, s);
@@ -482,30 +512,36 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
   const int sms = ctx->num_sms;
   constexpr int kSymMergeBin = kNumSymBins;
   const int nsb = kNumSymBins + 1;
-  long long* flop = sc.get<long long>(m);
-  int* lo = sc.get<int>(m);
-  int* hi = sc.get<int>(m);
-  uint8_t* symkey = sc.get<uint8_t>(m);
-  uint8_t* numkey = sc.get<uint8_t>(m);
-  int* row_nnz = sc.get<int>(m);
-  int* hslot = sc.get<int>(m);
-  int* rows_sym = sc.get<int>(m);
-  int* rows_num = sc.get<int>(m);
-  long long* crp = sc.get<long long>((size_t)m + 1);
-  unsigned long long* htop = sc.get<unsigned long long>(1);
-  long long* boff_sym = sc.get<long long>(kMaxBins + 1);
-  long long* boff_num = sc.get<long long>(kMaxBins + 1);
-  AnalyzeStats* gst = sc.get<AnalyzeStats>(1);
-  int* err = sc.get<int>(4);
-  long long* scs = sc.get<long long>(scan_scratch_elems(m));
-  void* pscr = sc.get<char>(partition_scratch_bytes(m, kMaxBins));
+  long long *flop, *boff_sym, *boff_num, *scs;
+  int *lo, *hi, *row_nnz, *hslot, *rows_sym, *rows_num, *err;
+  uint8_t *symkey, *numkey;
+  unsigned long long* htop;
+  AnalyzeStats* gst;
+  void* pscr;
+  sc.carve([&](Carver& c) {   // the three zero-initialised ones first: one memset clears them
+    gst = c.take<AnalyzeStats>(1);
+    err = c.take<int>(4);
+    htop = c.take<unsigned long long>(1);
+    flop = c.take<long long>(m);
+    lo = c.take<int>(m);
+    hi = c.take<int>(m);
+    symkey = c.take<uint8_t>(m);
+    numkey = c.take<uint8_t>(m);
+    row_nnz = c.take<int>(m);
+    hslot = c.take<int>(m);
+    rows_sym = c.take<int>(m);
+    rows_num = c.take<int>(m);
+    boff_sym = c.take<long long>(kMaxBins + 1);
+    boff_num = c.take<long long>(kMaxBins + 1);
+    scs = c.take<long long>(scan_scratch_elems(m));
+    pscr = c.take<char>(partition_scratch_bytes(m, kMaxBins));
+  });
+  long long* crp = sc.get<long long>((size_t)m + 1);   // handed to the caller with C
   if (sc.failed) {
     set_error("device pool allocation failed");
     return kErrOom;
   }
-  CK(cudaMemsetAsync(gst, 0, sizeof(AnalyzeStats), s));
-  CK(cudaMemsetAsync(err, 0, sizeof(int) * 4, s));
-  CK(cudaMemsetAsync(htop, 0, sizeof(unsigned long long), s));
+  CK(cudaMemsetAsync(gst, 0, (char*)(htop + 1) - (char*)gst, s));
   CK(cudaMemsetAsync(hslot, 0xff, sizeof(int) * (size_t)m, s));
 
   // arena for the bitmaps the symbolic bitmap tier hands to the numeric rank tier (rows that
