@@ -282,9 +282,21 @@ class DeviceResult:
 
     def __init__(self, out: CsrOut, stats: Stats):
         self._out = out
-        self.stats = stats.as_dict()
+        self._stats = stats
+        self._stats_dict = None
         self.rows, self.cols, self.nnz = int(out.rows), int(out.cols), int(out.nnz)
         self.row_ptr, self.col_idx, self.val = out.row_ptr, out.col_idx, out.val
+
+    @property
+    def stats(self) -> dict:
+        """The call's statistics as a dict (built on first access)."""
+        if self._stats_dict is None:
+            self._stats_dict = self._stats.as_dict()
+        return self._stats_dict
+
+    def phase_ms(self, phase: str) -> float:
+        """Device time of one phase of the call (with timing=True), without building the dict."""
+        return float(self._stats.ms_phase[PHASES.index(phase)])
 
     def free(self) -> None:
         if self._out is not None:

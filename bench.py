@@ -441,7 +441,8 @@ def main():
     rp_host = np.asarray(A.row_ptr, np.int64)
 
     def step():
-        """One pass over this rank's rows; returns (nnz, numeric ms, stats of the last block)."""
+        """One pass over this rank's rows; returns (nnz, numeric ms, the last block's result --
+        its statistics are read after the timed region)."""
         nnz_tot, num_ms, st = 0, 0.0, None
         for b0, b1 in zip(blocks[:-1], blocks[1:]):
             res = ap.spgemm_device(b1 - b0, cols, int(rp_host[b1] - rp_host[b0]),
@@ -449,8 +450,8 @@ def main():
                                    B=Bspec, op="ab", method=args.method, row_base=b0,
                                    stream=sptr, device=local, timing=True)
             nnz_tot += res.nnz
-            num_ms += res.stats["ms_phase"]["numeric"]
-            st = res.stats
+            num_ms += res.phase_ms("numeric")
+            st = res
             res.free()
         if world > 1:   # global row offsets of C: one all-gather, read on the host later
             D.exchange_nnz_into(dist, nnz_tot, nnz_all)
@@ -545,8 +546,9 @@ def main():
                          "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)"
                          if peaks["source"] == "measured" else "fallback 6.65 TB/s",
                          "traffic_source": tr_src},
-            "phase_ms": stats["ms_phase"] if stats else None,
-            "bin_rows": ({k: v for k, v in stats["bin_rows"].items() if v} if stats else None),
+            "phase_ms": stats.stats["ms_phase"] if stats else None,
+            "bin_rows": ({k: v for k, v in stats.stats["bin_rows"].items() if v}
+                         if stats else None),
             "clocks": clocks, "gpu_launches": launches,
             "e2e": e2e, "cpu_baseline": cpu,
         }
