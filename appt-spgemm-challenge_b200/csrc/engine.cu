@@ -281,7 +281,7 @@ static const char* kPhaseNames[8] = {"h2d", "transpose", "analyze", "symbolic",
                                      "scan", "numeric",   "d2h",     "other"};
 
 // ------------------------------------------------------------------ device pipeline
-constexpr int kSinkBlocks = 4;   // row blocks of the numeric phase when C goes to the host
+constexpr int kSinkBlocks = 8;   // row blocks of the numeric phase when C goes to the host
 
 // Host destination of C. With a sink, the numeric phase runs in row blocks and the copies of a
 // finished block go out on the copy stream while the next block computes; `alloc` is called
