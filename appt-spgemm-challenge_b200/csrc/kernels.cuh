@@ -120,6 +120,11 @@ struct AnalyzeStats {          // device-side global statistics (atomics)
 };
 
 // util.cu
+// Raises the dynamic shared-memory limit of kernel `kern` to `bytes` on the current device.
+// The attribute belongs to the device that is current when it is set, so it is applied once
+// per (kernel, device) -- and again if a launch asks for more -- under a mutex (callers on
+// several host threads or devices are safe).
+void smem_opt_in(const void* kern, size_t bytes);
 size_t scan_scratch_elems(long long n);
 // scans and partitions return the number of kernels they launched
 int scan_exclusive(const int* in, long long* out, long long n, long long* scratch, cudaStream_t s);

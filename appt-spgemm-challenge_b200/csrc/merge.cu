@@ -107,11 +107,7 @@ void run_merge(const int* rows, const long long* bin_off, int bin, long long nro
   constexpr int WPB = 4;
   const size_t smem = (size_t)WPB * 3 * kMergeMaxLists * sizeof(int);
   auto kern = merge_kernel<NUMERIC, WPB>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  smem_opt_in((const void*)kern, smem);
   int occ = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, WPB * 32, smem);
   if (occ < 1) occ = 1;

@@ -19,7 +19,9 @@
 // any stream capture. Every call uses the same array and leaves its contents there; everything
 // a call relies on being zero it clears itself. Calls whose GPU work overlapped would race on the
 // array: this function serialises its callers per device on the host and returns only after its
-// own GPU work has finished, so calls made through it do not overlap.
+// own GPU work has finished, so calls made through it do not overlap. Each call blocks its host
+// thread: it reads nnz(C) back in the middle (a stream synchronisation) and synchronises the
+// stream again before it returns.
 // This entry point has no counterpart in the reference.
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -94,9 +96,11 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
     set_error("appt_spgemm_noalloc: null output buffer or negative capacity");
     return kErrInvalid;
   }
-  if (A.rows < 0 || A.cols < 0 || A.nnz < 0 || A.rows >= (1ll << 31) - 1 ||
-      A.nnz >= (1ll << 31) - 1 || !A.rp || (A.nnz > 0 && (!A.ci || !A.val))) {
-    set_error("appt_spgemm_noalloc: invalid A");
+  // every size is narrowed to int32 for the kernels: reject what does not fit
+  auto fits = [](long long x) { return x >= 0 && x < (1ll << 31) - 1; };
+  if (!fits(A.rows) || !fits(A.cols) || !fits(A.nnz) || !A.rp ||
+      (A.nnz > 0 && (!A.ci || !A.val))) {
+    set_error("appt_spgemm_noalloc: invalid A (sizes must lie in [0, 2^31 - 1), pointers set)");
     return kErrInvalid;
   }
   const MatView B = Bp ? *Bp : A;
@@ -104,8 +108,13 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
     set_error("appt_spgemm_noalloc: C = A*A needs a square A");
     return kErrInvalid;
   }
-  if (A.cols != B.rows || !B.rp || (B.nnz > 0 && (!B.ci || !B.val))) {
-    set_error("appt_spgemm_noalloc: A.cols != B.rows or invalid B");
+  if (!fits(B.rows) || !fits(B.cols) || !fits(B.nnz) || !B.rp ||
+      (B.nnz > 0 && (!B.ci || !B.val))) {
+    set_error("appt_spgemm_noalloc: invalid B (sizes must lie in [0, 2^31 - 1), pointers set)");
+    return kErrInvalid;
+  }
+  if (A.cols != B.rows) {
+    set_error("appt_spgemm_noalloc: A.cols != B.rows");
     return kErrInvalid;
   }
   const long long max_rows = noalloc_max_rows();
@@ -176,6 +185,13 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
   launch_classify_numeric(dA, m, kMethodAdaptive, flop, lo, hi, row_nnz, numkey, sms, s);
   launched += partition_rows(numkey, m, kNumNumBins, rows_num, boff_num, pscr, s);
   note_launches(launched);
+  // A launch that failed left the array holding the previous call's row counts and bin lists:
+  // stop before anything is read back from it.
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("appt_spgemm_noalloc: launch failed: ") + cudaGetErrorString(e));
+    return kErrCuda;
+  }
 
   long long nnz = 0;
   long long boff[kNumNumBins + 1];
@@ -212,9 +228,9 @@ int spgemm_noalloc(const MatView& A, const MatView* Bp, long long* crp, int* cci
                    DenseRows{}, crp, cci, cval, err + 4 + b, err, sms, s);
     note_launches(1);
   }
-  e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("appt_spgemm_noalloc: ") + cudaGetErrorString(e));
     return kErrCuda;

@@ -676,11 +676,7 @@ void run_warp_hash(int bin, const int* rows, const long long* bin_off, long long
                    int* err, int num_sms, cudaStream_t s) {
   const size_t smem = (size_t)WPB * T * (sizeof(double) + sizeof(int));
   auto kern = num_warp_hash_kernel<T, WPB>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  smem_opt_in((const void*)kern, smem);
   const int grid = occupancy_grid(kern, WPB * 32, smem, num_sms, nrows, WPB);
   kern<<<grid, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, crp, cci, cval,
                                     err);
@@ -693,11 +689,7 @@ void run_warp_rank_g(int bin, const int* rows, const long long* bin_off, long lo
                      double* cval, int* err, int num_sms, cudaStream_t s) {
   const size_t smem = (size_t)WPB * BUDGET;
   auto kern = num_warp_rank_kernel<BUDGET, WPB, G>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  smem_opt_in((const void*)kern, smem);
   const int grid = occupancy_grid(kern, WPB * 32, smem, num_sms, nrows, WPB);
   kern<<<grid, WPB * 32, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, lo, hi, handoff,
                                     crp, cci, cval, err);
@@ -775,11 +767,7 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
       constexpr int NT = 512;
       const size_t smem = (size_t)kHashBlockSlots * (8 + 4) + (size_t)NT * (8 + 8 + 4);
       auto kern = num_block_hash_kernel<kHashBlockSlots, NT>;
-      static bool attr = false;
-      if (!attr) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-      }
+      smem_opt_in((const void*)kern, smem);
       const int grid = occupancy_grid(kern, NT, smem, num_sms, nrows, 1);
       kern<<<grid, NT, smem, s>>>(rows, bin_off, bin, A, B, upper, row_base, crp, cci, cval,
                                   row_counter, err);
@@ -789,11 +777,7 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
       constexpr int NT = 1024, MAXW = 32768;
       const size_t smem = (size_t)MAXW * 6 + (size_t)NT * (4 + 8 + 12);
       auto kern = num_block_rank_kernel<NT, MAXW>;
-      static bool attr = false;
-      if (!attr) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-      }
+      smem_opt_in((const void*)kern, smem);
       const long long grid = nrows < num_sms ? nrows : num_sms;
       kern<<<(unsigned)grid, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, crp, cci, cval,
                                             row_counter, err);
@@ -805,11 +789,7 @@ void launch_numeric(int bin, const int* rows, const long long* bin_off, long lon
       const size_t smem = (size_t)WC * 8 + (size_t)(WC / 32) * 4 + (size_t)NT * (8 + 12 + 4) +
                           (size_t)kWindowSplit * 4;
       auto kern = num_block_window_kernel<WC, NT>;
-      static bool attr = false;
-      if (!attr) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-      }
+      smem_opt_in((const void*)kern, smem);
       const long long grid = nrows < 2 * num_sms ? nrows : 2 * num_sms;
       kern<<<(unsigned)grid, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, dense, crp, cci,
                                             cval, row_counter, err);

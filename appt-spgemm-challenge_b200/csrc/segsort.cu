@@ -224,14 +224,8 @@ void segsort(int* keys, double* vals, int* keys_alt, double* vals_alt, const lon
   }
   {
     const size_t smem = (size_t)kSegBlockCap * 16;
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(segsort_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-      cudaFuncSetAttribute(segsort_large_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-      attr = true;
-    }
+    smem_opt_in((const void*)segsort_block_kernel, smem);
+    smem_opt_in((const void*)segsort_large_kernel, smem);
     segsort_block_kernel<<<num_sms * 2, kSegNT, smem, s>>>(keys, vals, off, segs, bin_off, 1);
     if (keys_alt && vals_alt)
       segsort_large_kernel<<<num_sms, kSegNT, smem, s>>>(keys, vals, keys_alt, vals_alt, off, segs,

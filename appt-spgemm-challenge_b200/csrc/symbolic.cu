@@ -218,11 +218,7 @@ void launch_sym_bitmap_g(int bin, const int* rows, const long long* bin_off, Csr
                          int num_sms, cudaStream_t s) {
   const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
   auto kern = sym_warp_bitmap_kernel<WORDS, WPB, G>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set = true;
-  }
+  smem_opt_in((const void*)kern, smem);
   int occ = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, WPB * 32, smem);
   if (occ < 1) occ = 1;
@@ -328,11 +324,7 @@ void launch_sym_warp(int bin, const int* rows, const long long* bin_off, Csr A, 
                      int* row_nnz, int* err, int num_sms, cudaStream_t s) {
   const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
   auto kern = sym_warp_kernel<WORDS, WPB>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set = true;
-  }
+  smem_opt_in((const void*)kern, smem);
   int occ = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, WPB * 32, smem);
   if (occ < 1) occ = 1;
@@ -433,11 +425,7 @@ void run_sym_small(Csr A, Csr B, int upper, int row_base, int* lo, int* hi, int*
   constexpr int WORDS = 1536, WPB = 8;
   const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
   auto kern = sym_small_kernel<WORDS, WPB, G>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set = true;
-  }
+  smem_opt_in((const void*)kern, smem);
   long long blocks = ((long long)A.rows + WPB - 1) / WPB;
   if (blocks > (long long)num_sms * 4) blocks = (long long)num_sms * 4;
   if (blocks < 1) blocks = 1;
@@ -556,11 +544,7 @@ void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, 
       constexpr int NT = 1024;
       const size_t smem = (size_t)kSymBlockWords * 4 + (size_t)NT * (8 + 12 + 4);
       auto kern = sym_block_kernel<NT, kSymBlockWords>;
-      static bool attr_set = false;
-      if (!attr_set) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr_set = true;
-      }
+      smem_opt_in((const void*)kern, smem);
       kern<<<num_sms, NT, smem, s>>>(rows, bin_off, bin, A, B, lo, hi, dense, row_nnz,
                                      row_counter);
       break;

@@ -7,6 +7,10 @@
 // Differences: offsets are int64 (the reference's int totals overflow past 2^31 products),
 // and the partition is stable (rows stay ascending inside a bin, which keeps neighbouring
 // rows -- which share B rows on banded/stencil inputs -- on neighbouring warps for L2 reuse).
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -293,6 +297,24 @@ void narrow_rowptr(const long long* in, int* out, long long n, cudaStream_t s) {
 void iota(int* out, int n, cudaStream_t s) {
   if (n <= 0) return;
   iota_kernel<<<(n + 255) / 256, 256, 0, s>>>(out, n);
+}
+
+void smem_opt_in(const void* kern, size_t bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;   // (kernel, device) -> bytes set
+  std::lock_guard<std::mutex> g(mu);
+  size_t& have = done[{kern, dev}];
+  if (have >= bytes) return;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+      cudaSuccess)
+    have = bytes;
+  else
+    cudaGetLastError();   // the launch that follows reports the failure
 }
 
 }  // namespace appt

@@ -55,3 +55,62 @@ def gpu_available() -> bool:
         return appt_spgemm.device_count() > 0
     except Exception:
         return False
+
+
+# ----------------------------------------------------------------------------- tier-forcing inputs
+def _csr():
+    from appt_spgemm.matrices import Csr
+    return Csr
+
+
+def tier_matrix_rows(n=1 << 18, seed=5):
+    """Rows of very different lengths so that every symbolic and numeric tier is used."""
+    Csr = _csr()
+    rng = np.random.default_rng(seed)
+    lens = np.minimum(rng.zipf(1.6, n), 700).astype(np.int64)
+    lens[:4] = [600, 300, 150, 2000]
+    lens[np.arange(4, n, 97)] = 0
+    rows = []
+    for i in range(n):
+        L = int(lens[i])
+        if L == 0:
+            rows.append(np.zeros(0, np.int64))
+            continue
+        if i % 3 == 0:   # banded rows (dense tier candidates)
+            c = np.unique(np.clip(i + rng.integers(-300, 300, L), 0, n - 1))
+        else:
+            c = np.unique(rng.integers(0, n, L))
+        rows.append(c)
+    rp = np.zeros(n + 1, np.int64)
+    rp[1:] = np.cumsum([len(r) for r in rows])
+    ci = np.concatenate(rows).astype(np.int32)
+    return Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))
+
+
+def hub_matrix(n=1 << 17, hubs=24, hub_len=6000, seed=9):
+    """Sparse rows plus a few hub rows with thousands of entries spread over the whole column
+    range: rows of A*A that reach a hub have more than 4096 entries on a sparse, wide span (the
+    CTA rank tier); the hub rows themselves span up to 2^17 columns."""
+    Csr = _csr()
+    rng = np.random.default_rng(seed)
+    rows = []
+    hub_ids = rng.choice(n, hubs, replace=False)
+    for i in range(n):
+        L = hub_len if i in hub_ids else int(rng.integers(1, 6))
+        rows.append(np.unique(rng.integers(0, n, L)))
+    rp = np.zeros(n + 1, np.int64)
+    rp[1:] = np.cumsum([len(r) for r in rows])
+    ci = np.concatenate(rows).astype(np.int32)
+    return Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))
+
+
+def window_matrix(n=8192, seed=8):
+    """Rows of A*A with more than ~600 entries packed into at most 16384 columns (the dense
+    window tier)."""
+    Csr = _csr()
+    rng = np.random.default_rng(seed)
+    rows = [np.unique(np.clip(i + rng.integers(-2000, 2000, 800), 0, n - 1)) for i in range(n)]
+    rp = np.zeros(n + 1, np.int64)
+    rp[1:] = np.cumsum([len(r) for r in rows])
+    ci = np.concatenate(rows).astype(np.int32)
+    return Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))

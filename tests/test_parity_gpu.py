@@ -6,7 +6,8 @@ Structure (row_ptr, col_idx) must be bit-exact; values within
 import numpy as np
 import pytest
 
-from conftest import abs_product, assert_same_structure, assert_values_close
+from conftest import (abs_product, assert_same_structure, assert_values_close, hub_matrix,
+                      tier_matrix_rows, window_matrix)
 
 pytestmark = pytest.mark.gpu
 
@@ -73,32 +74,9 @@ def test_workload_families_small(name, method):
         check(A, op="aat_upper", method=method)
 
 
-def _tier_matrix(n=1 << 18, seed=5):
-    """Rows of very different lengths so that every symbolic and numeric tier is used."""
-    rng = np.random.default_rng(seed)
-    lens = np.minimum(rng.zipf(1.6, n), 700).astype(np.int64)
-    lens[:4] = [600, 300, 150, 2000]
-    lens[np.arange(4, n, 97)] = 0
-    rows = []
-    for i in range(n):
-        L = int(lens[i])
-        if L == 0:
-            rows.append(np.zeros(0, np.int64))
-            continue
-        if i % 3 == 0:   # banded rows (dense tier candidates)
-            c = np.unique(np.clip(i + rng.integers(-300, 300, L), 0, n - 1))
-        else:
-            c = np.unique(rng.integers(0, n, L))
-        rows.append(c)
-    rp = np.zeros(n + 1, np.int64)
-    rp[1:] = np.cumsum([len(r) for r in rows])
-    ci = np.concatenate(rows).astype(np.int32)
-    return M.Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))
-
-
 @pytest.fixture(scope="module")
 def tier_matrix():
-    return _tier_matrix()
+    return tier_matrix_rows()
 
 
 @pytest.mark.parametrize("method", ["adaptive", "hash", "merge"])
@@ -113,25 +91,9 @@ def test_all_tiers(tier_matrix, method):
         assert "merge" in used and "window" in used, used
 
 
-def _hub_matrix(n=1 << 17, hubs=24, hub_len=6000, seed=9):
-    """Sparse rows plus a few hub rows with thousands of entries spread over the whole column
-    range: rows of A*A that reach a hub have more than 4096 entries on a sparse, wide span (the
-    CTA rank tier); the hub rows themselves span up to 2^17 columns."""
-    rng = np.random.default_rng(seed)
-    rows = []
-    hub_ids = rng.choice(n, hubs, replace=False)
-    for i in range(n):
-        L = hub_len if i in hub_ids else int(rng.integers(1, 6))
-        rows.append(np.unique(rng.integers(0, n, L)))
-    rp = np.zeros(n + 1, np.int64)
-    rp[1:] = np.cumsum([len(r) for r in rows])
-    ci = np.concatenate(rows).astype(np.int32)
-    return M.Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))
-
-
 @pytest.mark.parametrize("op", ["ab", "aat_upper"])
 def test_block_rank_tier(op):
-    A = _hub_matrix()
+    A = hub_matrix()
     C, st = check(A, op=op)
     assert st["tier_rows"]["block_rank"] > 0, st["tier_rows"]
 
@@ -171,14 +133,7 @@ def test_host_results_views_and_pinned_reuse():
 def test_window_tier_dense_rows():
     """Rows of C with more than ~600 entries packed into at most 16384 columns take the dense
     window tier."""
-    rng = np.random.default_rng(8)
-    n = 8192
-    rows = [np.unique(np.clip(i + rng.integers(-2000, 2000, 800), 0, n - 1)) for i in range(n)]
-    rp = np.zeros(n + 1, np.int64)
-    rp[1:] = np.cumsum([len(r) for r in rows])
-    ci = np.concatenate(rows).astype(np.int32)
-    A = M.Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))
-    C, st = check(A)
+    C, st = check(window_matrix())
     assert st["tier_rows"]["window"] > 0, st["tier_rows"]
 
 
