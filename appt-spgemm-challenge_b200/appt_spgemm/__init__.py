@@ -92,7 +92,8 @@ class Stats(ct.Structure):
 class Options(ct.Structure):
     _fields_ = [("op", ct.c_int32), ("method", ct.c_int32), ("in_mem", ct.c_int32),
                 ("out_mem", ct.c_int32), ("row_base", ct.c_int64), ("stream", ct.c_void_p),
-                ("device", ct.c_int32), ("timing", ct.c_int32)]
+                ("device", ct.c_int32), ("timing", ct.c_int32), ("b_mem", ct.c_int32),
+                ("reserved", ct.c_int32)]
 
 
 class ApptError(RuntimeError):
@@ -137,6 +138,8 @@ def load() -> ct.CDLL:
     lib.appt_reference_score.restype = ct.c_double
     lib.appt_last_error.restype = ct.c_char_p
     lib.appt_device_count.restype = ct.c_int
+    lib.appt_release_cached.argtypes = [ct.c_int]
+    lib.appt_release_cached.restype = ct.c_int
     lib.appt_kernel_launches.restype = ct.c_int64
     lib.appt_version.restype = ct.c_char_p
     lib.appt_default_options.argtypes = [ct.POINTER(Options)]
@@ -159,6 +162,25 @@ def load() -> ct.CDLL:
                               ct.POINTER(ct.c_void_p)]
     lib.build_csc.restype = None
     lib.mempool_cap.restype = ct.c_size_t
+    vp, i64p = ct.c_void_p, ct.POINTER(ct.c_int64)
+    lib.appt_split_rows.argtypes = [vp, ct.c_int64, ct.c_int, vp]
+    lib.appt_split_rows.restype = ct.c_int
+    lib.appt_comm_unique_id.argtypes = [vp]
+    lib.appt_comm_unique_id.restype = ct.c_int
+    lib.appt_comm_init.argtypes = [vp, ct.c_int, ct.c_int, ct.c_int, ct.POINTER(vp)]
+    lib.appt_comm_init.restype = ct.c_int
+    lib.appt_comm_destroy.argtypes = [vp]
+    lib.appt_comm_destroy.restype = ct.c_int
+    lib.appt_comm_broadcast_csr.argtypes = [vp, ct.c_int, ct.POINTER(CsrIn), ct.POINTER(ct.c_double)]
+    lib.appt_comm_broadcast_csr.restype = ct.c_int
+    lib.appt_comm_free_csr.argtypes = [vp, ct.POINTER(CsrIn)]
+    lib.appt_comm_free_csr.restype = ct.c_int
+    lib.appt_comm_row_split.argtypes = [vp, ct.c_int, ct.POINTER(CsrIn), ct.POINTER(CsrIn), vp]
+    lib.appt_comm_row_split.restype = ct.c_int
+    lib.appt_comm_spgemm.argtypes = [vp, ct.POINTER(CsrIn), ct.POINTER(CsrIn), ct.POINTER(Options),
+                                     ct.POINTER(CsrOut), vp, ct.POINTER(Stats)]
+    lib.appt_comm_spgemm.restype = ct.c_int
+    del i64p
     lib.mempool_used.restype = ct.c_size_t
     _lib = lib
     return lib
@@ -170,6 +192,11 @@ def last_error() -> str:
 
 def device_count() -> int:
     return int(load().appt_device_count())
+
+
+def release_cached(device: int = 0) -> None:
+    """Return the library's cached pool memory on `device` to the driver."""
+    _check(load().appt_release_cached(device), "appt_release_cached")
 
 
 def kernel_launches() -> int:
@@ -194,9 +221,13 @@ def _host_in(A: Csr, keep: list) -> CsrIn:
                  va.ctypes.data)
 
 
+B_AS_A, B_HOST, B_DEVICE = 0, 1, 2
+
+
 def _options(op="ab", method="adaptive", in_mem=MEM_HOST, out_mem=MEM_HOST, row_base=0,
-             stream=None, device=0, timing=False) -> Options:
+             stream=None, device=0, timing=False, b_mem=B_AS_A) -> Options:
     o = Options()
+    o.b_mem = b_mem
     o.op = OPS[op] if isinstance(op, str) else int(op)
     o.method = METHODS[method] if isinstance(method, str) else int(method)
     o.in_mem, o.out_mem = in_mem, out_mem

@@ -1,37 +1,39 @@
-"""Row-sharded multi-GPU SpGEMM plumbing (one process per GPU, torch.distributed).
+"""Row-sharded multi-GPU SpGEMM: Python side of the library's multi-GPU C ABI (appt_comm_*).
 
-The reference is single-GPU (src/main.cu:44 pins device 0). Here rows of A are independent
-units: each rank computes a contiguous block of rows of C, the blocks balanced by
-intermediate-product count; B (or A^T) is replicated to every GPU once with an NCCL broadcast,
-and the only per-product collective is an all-gather of each rank's nnz(C block), from which
-every rank derives the global row offsets of its block. C stays sharded.
+The reference is single-GPU (src/main.cu:44 selects device 0). Here rows of A are independent
+units: one process per GPU computes a contiguous block of rows of C, the blocks balanced by
+intermediate-product count; B (or A^T) is replicated to every GPU once with NCCL broadcasts, and
+each product does one all-gather of the ranks' nnz(C block), from which every rank derives the
+global offset of its block. C stays sharded. All of that runs inside libappt_spgemm.so (C++ over
+NCCL, loaded at run time); this module only marshals arguments. Exchanging the 128-byte
+communicator id between processes is the caller's business (any host channel).
 
-Everything here is host-side logic on top of the C ABI; the per-rank compute is the engine's
-device-pointer entry point (appt_spgemm with APPT_MEM_DEVICE operands).
+Host-only helpers (split_rows, block_offsets, assemble_blocks) need no GPU.
 """
 from __future__ import annotations
 
+import ctypes as ct
+
 import numpy as np
 
+from . import (B_DEVICE, CsrIn, CsrOut, DeviceResult, MEM_DEVICE, MEM_HOST, Stats, _check,
+               _options, _take_host_out, _view_host_out, load)
+from .matrices import Csr
 
-def partition_rows(row_products: np.ndarray, world: int) -> list[int]:
-    """Contiguous row bounds [b_0 = 0, b_1, ..., b_world = rows] splitting the cumulative
-    products as evenly as contiguous blocks allow (prefix-balanced)."""
-    rows = int(row_products.shape[0])
-    if world <= 0:
-        raise ValueError("world must be positive")
-    cum = np.concatenate([[0], np.cumsum(np.asarray(row_products, dtype=np.int64))])
-    total = int(cum[-1])
-    bounds = [0]
-    for r in range(1, world):
-        target = total * r / world
-        b = int(np.searchsorted(cum, target, side="left"))
-        # take the closer of the two candidate cut points
-        if b > 0 and abs(cum[b - 1] - target) <= abs(cum[min(b, rows)] - target):
-            b -= 1
-        bounds.append(max(bounds[-1], min(b, rows)))
-    bounds.append(rows)
-    return bounds
+ID_BYTES = 128
+
+
+def split_rows(row_products, parts: int) -> list[int]:
+    """Contiguous row bounds [0 = b_0, b_1, ..., b_parts = rows] that split the per-row
+    intermediate products as evenly as contiguous blocks allow (appt_split_rows)."""
+    p = np.ascontiguousarray(row_products, dtype=np.int64)
+    out = np.zeros(int(parts) + 1, dtype=np.int64)
+    _check(load().appt_split_rows(p.ctypes.data if p.size else None, p.size, int(parts),
+                                  out.ctypes.data), "appt_split_rows")
+    return [int(x) for x in out]
+
+
+partition_rows = split_rows
 
 
 def block_offsets(nnz_per_rank) -> np.ndarray:
@@ -43,71 +45,122 @@ def block_offsets(nnz_per_rank) -> np.ndarray:
     return out
 
 
-def exchange_nnz(dist, my_nnz: int, device) -> np.ndarray:
-    """All-gather of every rank's int64 nnz (one collective); returns block_offsets()."""
-    import torch
-    world = dist.get_world_size()
-    mine = torch.tensor([int(my_nnz)], dtype=torch.int64, device=device)
-    parts = [torch.empty(1, dtype=torch.int64, device=device) for _ in range(world)]
-    dist.all_gather(parts, mine)
-    return block_offsets(torch.cat(parts).cpu().numpy())
-
-
-def exchange_nnz_into(dist, my_nnz: int, out) -> None:
-    """The same all-gather into a preallocated int64 tensor of world_size entries, without
-    waiting for it on the host (block_offsets(out.cpu().numpy()) gives the offsets later)."""
-    import torch
-    mine = torch.full((1,), int(my_nnz), dtype=torch.int64, device=out.device)
-    dist.all_gather_into_tensor(out, mine)
-
-
-def replicate(dist, tensors, src: int = 0) -> None:
-    """Broadcast operand arrays (already allocated with the right sizes on every rank)."""
-    for t in tensors:
-        dist.broadcast(t, src)
-
-
 def global_row_ptr(local_row_ptr: np.ndarray, offset: int) -> np.ndarray:
     """Row pointers of a block shifted to global entry positions."""
     return np.asarray(local_row_ptr, dtype=np.int64) + int(offset)
 
 
-def gather_csr(dist, bounds, cols: int, row_ptr, col_idx, val, offsets, dst: int = 0):
-    """Assemble the sharded C on rank `dst` with point-to-point transfers: every rank passes its
-    block (row_ptr relative to the block, starting at 0, as int64; col_idx int32; val float64 --
-    torch tensors on the rank's device for NCCL, on the CPU for gloo) and `offsets` from
-    exchange_nnz. Returns (row_ptr int64, col_idx, val) of the whole C on `dst`, None elsewhere.
-    All ranks must call it."""
-    import torch
-    rank, world = dist.get_rank(), dist.get_world_size()
-    if rank != dst:
-        dist.send(row_ptr.contiguous(), dst)
-        if int(offsets[rank + 1] - offsets[rank]) > 0:
-            dist.send(col_idx.contiguous(), dst)
-            dist.send(val.contiguous(), dst)
-        return None
+def assemble_blocks(bounds, cols: int, blocks, offsets) -> Csr:
+    """The whole C from the ranks' host blocks (each a Csr whose row_ptr starts at 0), in rank
+    order, placed at `offsets` (block_offsets of the ranks' nnz)."""
     rows = int(bounds[-1])
     total = int(offsets[-1])
-    dev = col_idx.device
-    rp = torch.empty(rows + 1, dtype=torch.int64, device=dev)
-    ci = torch.empty(total, dtype=torch.int32, device=dev)
-    va = torch.empty(total, dtype=torch.float64, device=dev)
-    for r in range(world):
+    rp = np.zeros(rows + 1, np.int64)
+    ci = np.zeros(total, np.int32)
+    va = np.zeros(total, np.float64)
+    for r, blk in enumerate(blocks):
         r0, r1 = int(bounds[r]), int(bounds[r + 1])
         e0, e1 = int(offsets[r]), int(offsets[r + 1])
-        if r == dst:
-            brp, bci, bva = row_ptr, col_idx, val
+        if blk.rows != r1 - r0 or blk.nnz != e1 - e0:
+            raise ValueError(f"block {r} does not match its bounds / offsets")
+        rp[r0:r1 + 1] = global_row_ptr(blk.row_ptr, e0)
+        ci[e0:e1] = blk.col_idx
+        va[e0:e1] = blk.val
+    return Csr(rows, cols, rp, ci, va)
+
+
+def _spec_in(spec) -> CsrIn:
+    rows, cols, nnz, rp, ci, va = spec
+    return CsrIn(int(rows), int(cols), int(nnz), rp, ci, va)
+
+
+class Communicator:
+    """One rank of a multi-GPU product (one process per GPU)."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ct.create_string_buffer(ID_BYTES)
+        _check(load().appt_comm_unique_id(buf), "appt_comm_unique_id")
+        return buf.raw
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, device: int):
+        if len(uid) != ID_BYTES:
+            raise ValueError("communicator id must be 128 bytes")
+        self.nranks, self.rank, self.device = int(nranks), int(rank), int(device)
+        self._h = ct.c_void_p()
+        idb = ct.create_string_buffer(uid, ID_BYTES)
+        _check(load().appt_comm_init(idb, self.nranks, self.rank, self.device,
+                                     ct.byref(self._h)), "appt_comm_init")
+
+    def destroy(self) -> None:
+        if self._h:
+            load().appt_comm_destroy(self._h)
+            self._h = ct.c_void_p()
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+    def broadcast_csr(self, root: int, spec=None):
+        """Replicate a device CSR (rows, cols, nnz, row_ptr, col_idx, val) held by `root`.
+        Returns (spec on this rank, transfer ms, owned): `owned` specs were allocated by the
+        library (release them with free_csr)."""
+        m = _spec_in(spec) if spec is not None else CsrIn()
+        ms = ct.c_double(0.0)
+        _check(load().appt_comm_broadcast_csr(self._h, int(root), ct.byref(m), ct.byref(ms)),
+               "appt_comm_broadcast_csr")
+        out = (int(m.rows), int(m.cols), int(m.nnz), m.row_ptr, m.col_idx, m.val)
+        return out, float(ms.value), self.rank != root
+
+    def free_csr(self, spec) -> None:
+        m = _spec_in(spec)
+        load().appt_comm_free_csr(self._h, ct.byref(m))
+
+    def row_split(self, root: int, A_spec=None, B_spec=None) -> list[int]:
+        """Row bounds of the ranks (nranks + 1), computed on the root from device-resident A
+        (and B; B = A when None) and broadcast."""
+        a = _spec_in(A_spec) if A_spec is not None else None
+        b = _spec_in(B_spec) if B_spec is not None else None
+        out = np.zeros(self.nranks + 1, np.int64)
+        _check(load().appt_comm_row_split(self._h, int(root), ct.byref(a) if a else None,
+                                          ct.byref(b) if b else None, out.ctypes.data),
+               "appt_comm_row_split")
+        return [int(x) for x in out]
+
+    def spgemm(self, A_block, B_spec, op: str = "ab", row_base: int = 0, out: str = "device",
+               method: str = "adaptive", stream=None, timing: bool = False, copy: bool = True):
+        """This rank's block of C. A_block: a host Csr, or a device spec tuple; B_spec: device
+        spec of the replicated B. Returns (result, block_offsets): result is a DeviceResult
+        (out="device") or a host Csr (out="host"; copy=False gives views of the library's
+        pinned block)."""
+        keep: list = []
+        if isinstance(A_block, Csr):
+            rp = np.ascontiguousarray(A_block.row_ptr, dtype=np.int32)
+            ci = np.ascontiguousarray(A_block.col_idx, dtype=np.int32)
+            va = np.ascontiguousarray(A_block.val, dtype=np.float64)
+            keep += [rp, ci, va]
+            a = CsrIn(A_block.rows, A_block.cols, int(rp[-1] - rp[0]), rp.ctypes.data,
+                      ci.ctypes.data, va.ctypes.data)
+            in_mem = MEM_HOST
         else:
-            brp = torch.empty(r1 - r0 + 1, dtype=torch.int64, device=dev)
-            dist.recv(brp, r)
-            bci, bva = None, None
-            if e1 > e0:
-                bci = torch.empty(e1 - e0, dtype=torch.int32, device=dev)
-                bva = torch.empty(e1 - e0, dtype=torch.float64, device=dev)
-                dist.recv(bci, r)
-                dist.recv(bva, r)
-        rp[r0:r1 + 1] = brp.to(dev) + e0
-        if e1 > e0:
-            ci[e0:e1] = bci
-            va[e0:e1] = bva
-    return rp, ci, va
+            a = _spec_in(A_block)
+            in_mem = MEM_DEVICE
+        b = _spec_in(B_spec)
+        o = _options(op, method, in_mem, MEM_HOST if out == "host" else MEM_DEVICE, row_base,
+                     stream, self.device, timing, b_mem=B_DEVICE)
+        res = CsrOut()
+        st = Stats()
+        offs = np.zeros(self.nranks + 1, np.int64)
+        _check(load().appt_comm_spgemm(self._h, ct.byref(a), ct.byref(b), ct.byref(o),
+                                       ct.byref(res), offs.ctypes.data, ct.byref(st)),
+               "appt_comm_spgemm")
+        if out == "host":
+            if not copy:
+                return _view_host_out(res), offs
+            try:
+                return _take_host_out(res), offs
+            finally:
+                load().appt_free_out(ct.byref(res))
+        return DeviceResult(res, st), offs

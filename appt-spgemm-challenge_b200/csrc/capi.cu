@@ -32,6 +32,7 @@ CallOptions opts_of(const appt_options* o) {
     c.stream = o->stream;
     c.device = o->device;
     c.timing = o->timing;
+    c.b_mem = o->b_mem;
   }
   return c;
 }
@@ -55,6 +56,19 @@ void export_out(const MatOut& m, appt_csr_out* C) {
 }
 
 }  // namespace
+
+static void export_stats(const CallStats& st, appt_stats* stats) {
+  if (!stats) return;
+  std::memset(stats, 0, sizeof(*stats));
+  stats->products = st.products;
+  stats->c_nnz = st.c_nnz;
+  for (int i = 0; i < APPT_NUM_BINS; ++i) stats->bin_rows[i] = st.bin_rows[i];
+  stats->ms_total = st.ms_total;
+  for (int i = 0; i < 8; ++i) stats->ms_phase[i] = st.ms_phase[i];
+  stats->kernel_launches = st.launches;
+  stats->method_used = st.method_used;
+}
+
 
 extern "C" {
 
@@ -181,18 +195,33 @@ int appt_spgemm(const appt_csr* A, const appt_csr* B, const appt_options* opt, a
   MatOut m;
   CallStats st;
   const int rc = appt::spgemm(a, B ? &b : nullptr, o, &m, &st);
-  if (stats) {
-    std::memset(stats, 0, sizeof(*stats));
-    stats->products = st.products;
-    stats->c_nnz = st.c_nnz;
-    for (int i = 0; i < APPT_NUM_BINS; ++i) stats->bin_rows[i] = st.bin_rows[i];
-    stats->ms_total = st.ms_total;
-    for (int i = 0; i < 8; ++i) stats->ms_phase[i] = st.ms_phase[i];
-    stats->kernel_launches = st.launches;
-    stats->method_used = st.method_used;
-  }
+  export_stats(st, stats);
   if (rc != APPT_OK) return rc;
   export_out(m, C);
+  return APPT_OK;
+}
+
+int appt_comm_spgemm(appt_comm* comm, const appt_csr* A_block, const appt_csr* B,
+                     const appt_options* opt, appt_csr_out* C_block, int64_t* block_offsets,
+                     appt_stats* stats) {
+  if (!comm || !A_block || !C_block || !block_offsets) {
+    appt::set_error("null argument");
+    return APPT_ERR_INVALID;
+  }
+  std::memset(C_block, 0, sizeof(*C_block));
+  appt_options def;
+  appt_default_options(&def);
+  const CallOptions o = opts_of(opt ? opt : &def);
+  MatView a = view_of(A_block);
+  MatView b;
+  if (B) b = view_of(B);
+  MatOut m;
+  CallStats st;
+  const int rc = appt::comm_spgemm(comm->c, a, B ? &b : nullptr, o, &m,
+                                   reinterpret_cast<long long*>(block_offsets), &st);
+  export_stats(st, stats);
+  if (rc != APPT_OK) return rc;
+  export_out(m, C_block);
   return APPT_OK;
 }
 
@@ -261,6 +290,7 @@ double appt_reference_score(const int32_t* row_ptr, int64_t rows, int64_t nnz) {
 
 const char* appt_last_error(void) { return appt::last_error(); }
 int appt_device_count(void) { return appt::device_count(); }
+int appt_release_cached(int device) { return appt::release_cached(device); }
 int64_t appt_kernel_launches(void) { return appt::kernel_launches(); }
 const char* appt_version(void) { return "appt-spgemm-b200 0.1 (sm_100a)"; }
 

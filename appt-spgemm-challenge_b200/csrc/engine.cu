@@ -281,6 +281,12 @@ static const char* kPhaseNames[8] = {"h2d", "transpose", "analyze", "symbolic",
                                      "scan", "numeric",   "d2h",     "other"};
 
 // ------------------------------------------------------------------ device pipeline
+// Called once per pipeline run with nnz(C), right after the mid-pipeline synchronisation that
+// learns it and before the numeric phase (multi-GPU calls post their nnz exchange from here).
+using NnzHook = std::function<int(long long)>;
+
+static int notify_nnz(const NnzHook* hook, long long nnz) { return hook ? (*hook)(nnz) : kOk; }
+
 constexpr int kSinkBlocks = 8;   // row blocks of the numeric phase when C goes to the host
 
 // Host destination of C. With a sink, the numeric phase runs in row blocks and the copies of a
@@ -311,7 +317,8 @@ static int lanes_per_row(long long nnz, long long rows) {
 }
 
 static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
-                      cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C, CallStats* st) {
+                      cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C, CallStats* st,
+                      const NnzHook* on_nnz) {
   const int m = A.rows;
   const int sms = ctx->num_sms;
   long long* flop = sc.get<long long>(m);
@@ -370,6 +377,8 @@ static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, 
   CK(cudaStreamSynchronize(s));
   long long nnz;
   std::memcpy(&nnz, ctx->stage, 8);
+  const int hrc = notify_nnz(on_nnz, nnz);
+  if (hrc) return hrc;
   int* cci = sc.get<int>(nnz);
   double* cval = sc.get<double>(nnz);
   if (sc.failed) {
@@ -404,7 +413,7 @@ constexpr long long kSmallNnz = 1 << 21;
 
 static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
                         cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C, CallStats* st,
-                        bool* fallback, cudaEvent_t vals_ready) {
+                        bool* fallback, cudaEvent_t vals_ready, const NnzHook* on_nnz) {
   *fallback = false;
   const int m = A.rows;
   const int sms = ctx->num_sms;
@@ -455,6 +464,8 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
     set_error("symbolic phase reported device error bits " + std::to_string(herr));
     return kErrDevice;
   }
+  const int hrc = notify_nnz(on_nnz, nnz);
+  if (hrc) return hrc;
   int* cci = sc.get<int>(nnz);
   double* cval = sc.get<double>(nnz);
   if (sc.failed) {
@@ -496,16 +507,16 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
 static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long long b_nnz,
                            int upper, int row_base, int method, cudaStream_t s, Scratch& sc,
                            PhaseTimer& tm, DevC* C, CallStats* st, HostSink* sink,
-                           cudaEvent_t vals_ready = nullptr) {
+                           cudaEvent_t vals_ready, const NnzHook* on_nnz) {
   if (method == kMethodEsc) {
     if (vals_ready) CK(cudaStreamWaitEvent(s, vals_ready, 0));
-    return esc_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st);
+    return esc_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st, on_nnz);
   }
   if (method == kMethodAdaptive && A.rows > 0 && A.rows <= kSmallRows && a_nnz <= kSmallNnz &&
       !env_flag("APPT_NO_SMALL_PATH")) {
     bool fallback = false;
     const int rc = small_device(ctx, A, B, a_nnz, upper, row_base, s, sc, tm, C, st, &fallback,
-                                vals_ready);
+                                vals_ready, on_nnz);
     if (rc != kOk || !fallback) return rc;
   }
   const int m = A.rows;
@@ -670,6 +681,10 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
   if (st) {
     st->products = (long long)hst.total_flop;
     for (int b = 0; b < kNumNumBins && b < 32; ++b) st->bin_rows[b] = boff[b + 1] - boff[b];
+  }
+  {
+    const int hrc = notify_nnz(on_nnz, nnz);
+    if (hrc) return hrc;
   }
   long long cstart[kSinkBlocks + 1];
   cstart[0] = 0;
@@ -880,8 +895,15 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
   int rc = check_view(A, opt.in_mem, "A");
   if (rc) return rc;
   const bool ab = opt.op == kOpAB || opt.op == kOpABUpper;
+  if (opt.b_mem < 0 || opt.b_mem > 2) {
+    set_error("bad b_mem");
+    return kErrInvalid;
+  }
+  // where B lives: with A unless b_mem says otherwise (a host row block of A against a B that is
+  // already resident on the device, as in multi-GPU calls)
+  const int b_in = opt.b_mem == 0 ? opt.in_mem : (opt.b_mem == 1 ? 0 : 1);
   if (B && ab) {
-    rc = check_view(*B, opt.in_mem, "B");
+    rc = check_view(*B, b_in, "B");
     if (rc) return rc;
   }
   Csr dA{}, dB{};
@@ -917,7 +939,7 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
         return kErrInvalid;
       }
       b_nnz = B->nnz;
-      if (opt.in_mem == 0) {
+      if (b_in == 0) {
         rc = stage_operand(*B, sc, s, &dB, vs);
         if (rc) return rc;
       } else {
@@ -947,7 +969,7 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
     CK(cudaEventRecord(vals.ev, vs));
   }
   return multiply_device(ctx, dA, dB, A.nnz, b_nnz, upper, (int)opt.row_base, opt.method, s, sc,
-                         tm, dc, st, sink, vals.ev);
+                         tm, dc, st, sink, vals.ev, opt.on_nnz);
 }
 
 // Pinned host blocks for results returned in host memory: a block released by free_out is kept
@@ -1420,6 +1442,18 @@ int estimate_row_nnz(const MatView& A, int att, int estimator, const CallOptions
   }
   if (m > 0) CK(cudaMemcpyAsync(out, est, sizeof(int) * (size_t)m, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
+  return kOk;
+}
+
+int release_cached(int device) {
+  DeviceCtx* ctx = nullptr;
+  int rc = get_ctx(device, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  CK(cudaSetDevice(device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  CK(cudaMemPoolTrimTo(ctx->pool, 0));
+  CK(cudaMemPoolTrimTo(ctx->pool_big, 0));
   return kOk;
 }
 

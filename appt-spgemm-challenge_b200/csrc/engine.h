@@ -3,6 +3,7 @@
 #pragma once
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <string>
 
 namespace appt {
@@ -57,6 +58,9 @@ struct CallOptions {
   void* stream = nullptr;
   int device = 0;
   int timing = 0;
+  int b_mem = 0;          // where B lives: 0 as in_mem, 1 host, 2 device
+  // called with nnz(C) once it is known, before the numeric phase (multi-GPU nnz exchange)
+  const std::function<int(long long)>* on_nnz = nullptr;
 };
 
 // Main entry: C = op(A, B). B may be null (B = A).
@@ -70,6 +74,8 @@ int row_products(const MatView& A, const MatView* B, const CallOptions& opt, lon
 // MinHash), 1 = MinHash, 2 = HyperLogLog
 int estimate_row_nnz(const MatView& A, int att, int estimator, const CallOptions& opt, int* out);
 double reference_score(const int* row_ptr, long long rows, long long nnz);
+// Returns the device's cached pool memory (freed temporaries and results) to the driver.
+int release_cached(int device);
 
 // spgemm.h-compatible flow: host buffer in the reference layout in, pinned host buffer in the
 // reference's C layout out. `att_quirk_cols` reports C_cols = A_cols as the reference's att_*.
@@ -95,6 +101,21 @@ size_t host_arena_cap();
 size_t host_arena_used();
 size_t devarena_used();
 
+// Multi-GPU (dist.cu): one communicator per process and GPU, NCCL loaded at run time.
+struct Comm;
+int comm_unique_id(void* id);
+int comm_init(const void* id, int nranks, int rank, int device, Comm** out);
+int comm_destroy(Comm* c);
+// Replicates a device CSR from `root`; non-root ranks get library-allocated arrays in *M
+// (*allocated = true).
+int comm_broadcast_csr(Comm* c, int root, MatView* M, bool* allocated, double* ms);
+int comm_row_split(Comm* c, int root, const MatView* A, const MatView* B, long long* bounds);
+// This rank's block of C; offsets[0 .. nranks] receives the ranks' first global entries.
+int comm_spgemm(Comm* c, const MatView& A, const MatView* B, CallOptions opt, MatOut* C,
+                long long* offsets, CallStats* st);
+// Prefix-balanced contiguous split of rows by their products count (host).
+int split_rows(const long long* products, long long rows, int parts, long long* bounds);
+
 void set_error(const std::string& msg);
 const char* last_error();
 int device_count();
@@ -102,3 +123,8 @@ long long kernel_launches();
 void note_launches(long long n);
 
 }  // namespace appt
+
+// Opaque communicator handle of the C ABI (include/appt_spgemm.h).
+struct appt_comm {
+  appt::Comm* c;
+};

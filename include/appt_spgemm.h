@@ -164,7 +164,14 @@ typedef struct appt_options {
   void *stream;     /* cudaStream_t; NULL = the library's stream for the device */
   int32_t device;   /* CUDA device ordinal */
   int32_t timing;   /* nonzero: record per-phase CUDA events into stats */
+  int32_t b_mem;    /* where B lives: APPT_B_AS_A (0, where in_mem says), APPT_B_HOST or
+                       APPT_B_DEVICE -- e.g. a host row block of A against a device-resident B */
+  int32_t reserved; /* 0 */
 } appt_options;
+
+#define APPT_B_AS_A 0
+#define APPT_B_HOST 1
+#define APPT_B_DEVICE 2
 
 /* Fill *opt with defaults: AB, adaptive, host in/out, device 0, row_base 0, no timing. */
 void appt_default_options(appt_options *opt);
@@ -226,8 +233,60 @@ int appt_spgemm_noalloc(const appt_csr *A, const appt_csr *B, int64_t *C_row_ptr
                         int32_t *C_col_idx, double *C_val, int64_t C_capacity,
                         int64_t *C_nnz_out, void *stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Multi-GPU: one process per GPU, rows of A sharded across the ranks, B replicated.
+ *
+ * The reference runs on one GPU (src/main.cu:44 selects device 0); these entry points are the
+ * row-sharded scaling of appt_spgemm. Rows of C are independent: each rank computes a contiguous
+ * block of rows (balanced by intermediate products) against a B that every rank holds. NCCL over
+ * NVLink carries only the replication of B and, per product, an all-gather of the ranks'
+ * nnz(C block) that gives every block its offset in the global C; C stays sharded. NCCL is
+ * loaded at run time (libnccl.so.2) by the first of these calls; waits on the other ranks are
+ * bounded by APPT_COMM_TIMEOUT_S seconds (default 300), after which the communicator is aborted
+ * and the call fails. Calls marked "collective" must be made by every rank, in the same order.
+ * ---------------------------------------------------------------------------------------- */
+#define APPT_COMM_ID_BYTES 128
+typedef struct appt_comm appt_comm;
+
+/* A fresh communicator id (APPT_COMM_ID_BYTES bytes, an NCCL unique id). One rank creates it and
+ * sends the bytes to the others over any host channel. */
+int appt_comm_unique_id(void *id);
+/* Joins the nranks-rank communicator named by id as `rank`, using CUDA device `device`.
+ * Collective. */
+int appt_comm_init(const void *id, int nranks, int rank, int device, appt_comm **out);
+int appt_comm_destroy(appt_comm *comm);
+/* Replicates a device-resident CSR from `root` to every rank: on the root M is read; on the other
+ * ranks the library allocates device arrays, fills them and stores them (and the sizes) in *M --
+ * release those with appt_comm_free_csr. *ms (may be NULL) receives the transfer's device time
+ * on this rank. Collective. */
+int appt_comm_broadcast_csr(appt_comm *comm, int root, appt_csr *M, double *ms);
+int appt_comm_free_csr(appt_comm *comm, appt_csr *M);
+/* Contiguous row bounds bounds[0 .. parts] (bounds[0] = 0, bounds[parts] = rows) that split the
+ * per-row intermediate products as evenly as contiguous blocks allow (each cut at the prefix
+ * nearest to r/parts of the total). Host only. */
+int appt_split_rows(const int64_t *row_products, int64_t rows, int parts, int64_t *bounds);
+/* The row split of C = A * B (B = A when NULL; both device-resident on `root`, may be NULL
+ * elsewhere) over the communicator's ranks: products counted on the root's GPU, bounds
+ * (nranks + 1 entries) broadcast to every rank. Collective. */
+int appt_comm_row_split(appt_comm *comm, int root, const appt_csr *A, const appt_csr *B,
+                        int64_t *bounds);
+/* This rank's block of C = op(A, B): A_block holds rows [opt->row_base, opt->row_base +
+ * A_block->rows) of A (where opt->in_mem says), B the whole of B (opt->b_mem may place it on the
+ * device while A_block is on the host). The C block is returned as by appt_spgemm;
+ * block_offsets[0 .. nranks] receives every rank's first entry in the global C (the last is
+ * nnz(C)). The nnz all-gather is posted as soon as this rank's nnz is known and overlaps its
+ * numeric phase. A rank whose call fails still takes part (and the others then fail with
+ * APPT_ERR_DEVICE). Collective. */
+int appt_comm_spgemm(appt_comm *comm, const appt_csr *A_block, const appt_csr *B,
+                     const appt_options *opt, appt_csr_out *C_block, int64_t *block_offsets,
+                     appt_stats *stats);
+
 const char *appt_last_error(void);
 int appt_device_count(void);
+/* Device memory that the library keeps cached for later calls (freed temporaries and released
+ * results stay in its stream-ordered pools) is returned to the driver. Waits for the device's
+ * library stream first. */
+int appt_release_cached(int device);
 int64_t appt_kernel_launches(void); /* kernels launched by this process so far */
 const char *appt_version(void);
 

@@ -85,6 +85,41 @@ int64_t oracle_symbolic(int64_t m, int64_t ncols, const int32_t *arp, const int3
   return total;
 }
 
+/* Per-row structure invariants of C for products too large to hold on the host: the exact
+ * number of distinct columns (as oracle_symbolic) and the sum of those distinct column ids. A
+ * matching (count, sum) pair per row is a size-independent check of the row's column set.
+ * Same product enumeration as oracle_symbolic (src/spgemm_kernel_manual.cu:121-159). */
+void oracle_symbolic_sums(int64_t m, int64_t ncols, const int32_t *arp, const int32_t *aci,
+                          const int32_t *brp, const int32_t *bci, int upper, int64_t row_base,
+                          int64_t *row_nnz, int64_t *row_colsum) {
+  int nt = oracle_num_threads();
+#pragma omp parallel num_threads(nt)
+  {
+    int64_t *mark = (int64_t *)malloc(sizeof(int64_t) * (size_t)(ncols > 0 ? ncols : 1));
+    for (int64_t j = 0; j < ncols; ++j) mark[j] = -1;
+#pragma omp for schedule(dynamic, 64)
+    for (int64_t i = 0; i < m; ++i) {
+      const int64_t ig = i + row_base;
+      int64_t cnt = 0, sum = 0;
+      for (int32_t p = arp[i]; p < arp[i + 1]; ++p) {
+        const int32_t k = aci[p];
+        for (int32_t q = brp[k]; q < brp[k + 1]; ++q) {
+          const int32_t j = bci[q];
+          if (upper && j < ig) continue;
+          if (mark[j] != i) {
+            mark[j] = i;
+            ++cnt;
+            sum += j;
+          }
+        }
+      }
+      row_nnz[i] = cnt;
+      row_colsum[i] = sum;
+    }
+    free(mark);
+  }
+}
+
 typedef struct {
   int32_t col;
   double val;

@@ -22,13 +22,13 @@ def pytest_configure(config):
 VALUE_RTOL = 1e-12
 
 
-def abs_product(A, B=None, op="ab"):
+def abs_product(A, B=None, op="ab", row_base=0):
     """|A| * |B| (same structure as the product), used as the per-entry error scale."""
     import oracle
     from appt_spgemm.matrices import Csr
     absA = Csr(A.rows, A.cols, A.row_ptr, A.col_idx, np.abs(A.val))
     absB = None if B is None else Csr(B.rows, B.cols, B.row_ptr, B.col_idx, np.abs(B.val))
-    return oracle.spgemm(absA, absB, op=op)
+    return oracle.spgemm(absA, absB, op=op, row_base=row_base)
 
 
 def assert_same_structure(C, R):
@@ -114,3 +114,54 @@ def window_matrix(n=8192, seed=8):
     rp[1:] = np.cumsum([len(r) for r in rows])
     ci = np.concatenate(rows).astype(np.int32)
     return Csr(n, n, rp.astype(np.int32), ci, rng.uniform(-1, 1, ci.size))
+
+
+# ----------------------------------------------------------------------------- device helpers
+class _CudaArray:
+    """Zero-copy view of library-owned device memory for torch (__cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (int(n),), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3,
+                                         "strides": None}
+
+
+def device_view(torch, ptr: int, n: int, dtype: str, device: int = 0):
+    """torch tensor over n elements of type dtype ('i4', 'i8', 'f8') at device address ptr."""
+    if n == 0:
+        return torch.zeros(0, dtype={"i4": torch.int32, "i8": torch.int64,
+                                     "f8": torch.float64}[dtype], device=f"cuda:{device}")
+    return torch.as_tensor(_CudaArray(ptr, n, "<" + dtype), device=f"cuda:{device}")
+
+
+def to_device(torch, A, device: int = 0):
+    """A's three arrays as device tensors (int32, int32, float64)."""
+    d = torch.device("cuda", device)
+    return (torch.from_numpy(np.ascontiguousarray(A.row_ptr, np.int32)).to(d),
+            torch.from_numpy(np.ascontiguousarray(A.col_idx, np.int32)).to(d),
+            torch.from_numpy(np.ascontiguousarray(A.val, np.float64)).to(d))
+
+
+def select_rows(A, rows):
+    """CSR of the listed rows of A (in the given order)."""
+    from appt_spgemm.matrices import Csr
+    rows = np.asarray(rows, np.int64)
+    rp = np.asarray(A.row_ptr, np.int64)
+    lens = rp[rows + 1] - rp[rows]
+    out_rp = np.zeros(rows.size + 1, np.int64)
+    np.cumsum(lens, out=out_rp[1:])
+    idx = segment_index(rp[rows], lens)
+    return Csr(int(rows.size), A.cols, out_rp.astype(np.int32), np.asarray(A.col_idx)[idx],
+               np.asarray(A.val)[idx])
+
+
+def segment_index(starts, lens):
+    """Concatenation of arange(s, s + l) for every (s, l) pair (int64)."""
+    starts = np.asarray(starts, np.int64)
+    lens = np.asarray(lens, np.int64)
+    total = int(lens.sum())
+    if total == 0:
+        return np.zeros(0, np.int64)
+    off = np.zeros(lens.size, np.int64)
+    np.cumsum(lens[:-1], out=off[1:])
+    return np.repeat(starts - off, lens) + np.arange(total, dtype=np.int64)
