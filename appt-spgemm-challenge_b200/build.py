@@ -83,6 +83,34 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     return LIB
 
 
+DRIVER = BUILD / "spgemm_test"
+
+
+def build_reference_driver(reference_dir, verbose: bool = False) -> Path | None:
+    """Links the reference's own driver (src/main.cu of a reference checkout, compiled here
+    unmodified) against libappt_spgemm.so in place of the reference's kernel objects and of
+    src/matrix_utils.cu: the drop-in check of the library's reference-compatible exports. The
+    executable is _build/spgemm_test (rpath to this directory). Returns None without the
+    reference sources."""
+    ref = Path(reference_dir)
+    main_cu = ref / "src" / "main.cu"
+    if not main_cu.exists():
+        return None
+    lib = build(verbose=verbose)
+    if DRIVER.exists() and DRIVER.stat().st_mtime >= max(lib.stat().st_mtime,
+                                                         main_cu.stat().st_mtime):
+        return DRIVER
+    cmd = [NVCC, *ARCH, "-O2", "-std=c++17", f"-I{ref / 'include'}", "-o", str(DRIVER),
+           str(main_cu), f"-L{PKG}", "-lappt_spgemm", "-Xlinker", "-rpath", "-Xlinker",
+           "$ORIGIN/..", "-lcudart"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"linking the reference driver failed:\n{r.stdout}\n{r.stderr}")
+    return DRIVER
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")

@@ -61,6 +61,8 @@ struct CallOptions {
   int b_mem = 0;          // where B lives: 0 as in_mem, 1 host, 2 device
   // called with nnz(C) once it is known, before the numeric phase (multi-GPU nnz exchange)
   const std::function<int(long long)>* on_nnz = nullptr;
+  // prefix of the per-phase lines printed when APPT_PROF=1 ("[<tag>] <phase> <ms> ms")
+  const char* prof_tag = "appt-prof";
 };
 
 // Main entry: C = op(A, B). B may be null (B = A).

@@ -79,6 +79,19 @@ void spgemm_transpose_product(void *A_buffer, int A_rows, int A_cols, int A_nnz,
 void build_csc(const int *d_row_ptr, const int *d_col_idx, const double *d_val, int A_rows,
                int A_nnz, int **col_ptr_out, int **row_idx_out, double **val_out);
 
+/* Matrix files for the reference's driver: read_matrix_market / write_matrix_market,
+ * print_matrix_info and verify_csr_matrices of src/matrix_utils.cu (include/spgemm.h:44-52) are
+ * exported with the reference's C++ linkage, so src/main.cu links without matrix_utils.cu. The
+ * reader also takes binary CSR files (8-byte magic "APPTCSR1", int64 rows/cols/nnz, int32
+ * row_ptr, int32 col_idx, fp64 val) with no parsing, and parses MatrixMarket text in one pass;
+ * the buffer layout and allocation (pinned when g_use_mempool, else malloc; release with
+ * host_free) are the reference's. These are the same functions with C linkage; a name ending in
+ * ".bin" makes the writer produce the binary form. */
+bool appt_read_matrix_file(const char *filename, void **buffer_out, int **row_ptr_out,
+                           int **col_idx_out, double **val_out, int *rows, int *cols, int *nnz);
+bool appt_write_matrix_file(const char *filename, const int *row_ptr, const int *col_idx,
+                            const double *val, int rows, int cols, int nnz);
+
 /* METHOD environment gating. Replaces should_run_method (spgemm.h:108,
  * src/spgemm_adaptive.cu:9-20). */
 bool should_run_method(const char *key);

@@ -7,18 +7,27 @@ oracle/Makefile) on seeded inputs from appt_spgemm.matrices and stores its outpu
   * workload-size cases: sha256 digests of row_ptr / col_idx plus value checksums and the full
     contents of 64 sampled rows (.json).
 
+Every run of the reference's hash path also prints the sum of its per-row output estimates
+("[hash] total_est=<n>" on stderr, src/spgemm_kernel_hash.cu:925); it is kept in each case's
+manifest entry (info.total_est). With --estimates the script instead runs the ESTIMATES cases --
+inputs with at least 100000 nonzeros, where the reference sizes rows by its MinHash (default) or
+HyperLogLog (EST_METHOD=hll) estimate rather than by exact products -- and writes only
+estimates.json with both sums per case.
+
 Needs a GPU (the reference is CUDA-only). Usage, from the repository root:
 
-  python tests/golden/make_golden.py --out gpurun_out/golden
+  python tests/golden/make_golden.py [--out DIR] [--estimates]
 
-then copy the files into tests/golden/. The inputs are regenerated from the same seeds by the
-tests, so only the reference's outputs are stored.
+DIR defaults to tests/golden. The inputs are regenerated from the same seeds by the tests, so
+only the reference's outputs are stored.
 """
 from __future__ import annotations
 
 import argparse
 import hashlib
 import json
+import os
+import re
 import subprocess
 import sys
 import tempfile
@@ -46,6 +55,18 @@ SMALL = {
     "banded_n4096": ("banded", {"n": 4096}, ["adaptive", "hash", "merge3"]),
     "rmat_s10": ("rmat", {"scale": 10}, ["adaptive", "hash", "merge3", "att_adaptive"]),
 }
+# Estimator pins: (generator, kwargs, reference method). All have >= 100000 nonzeros.
+ESTIMATES = {
+    "stencil27_g24": ("stencil27", {"g": 24}, "hash"),
+    "stencil27_g40": ("stencil27", {"g": 40}, "hash"),
+    "stencil27_g64": ("stencil27", {}, "hash"),
+    "uniform8_n32768": ("uniform8", {"n": 32768}, "hash"),
+    "banded_n32768": ("banded", {"n": 32768}, "hash"),
+    "rmat_s14": ("rmat", {"scale": 14}, "hash"),
+    "random_3000": ("random_csr", {"rows": 3000, "cols": 3000, "density": 0.02, "seed": 31},
+                    "hash"),
+    "stencil27_g24_att": ("stencil27", {"g": 24}, "att_hash"),
+}
 LARGE = {
     "uniform8_n4096": ("uniform8", {}, ["adaptive", "merge3", "hash"]),
     "stencil27_g64": ("stencil27", {}, ["adaptive", "hash"]),
@@ -57,16 +78,29 @@ def gen(name: str, kw: dict) -> M.Csr:
     return getattr(M, name)(**kw)
 
 
-def run_ref(method: str, A: M.Csr, td: Path):
+def total_est(stderr: str):
+    """The last "[hash] total_est=<n>" the reference printed, or None."""
+    m = re.findall(r"\[hash\] total_est=(-?\d+)", stderr)
+    return int(m[-1]) if m else None
+
+
+def run_ref(method: str, A: M.Csr, td: Path, est_method: str | None = None):
     inp = td / "in.bin"
     out = td / "out.bin"
     M.save_bin(inp, A)
     if out.exists():
         out.unlink()
+    env = dict(os.environ)
+    env.pop("EST_METHOD", None)
+    if est_method:
+        env["EST_METHOD"] = est_method
     r = subprocess.run([str(REF), method, str(inp), "--out", str(out), "--warmup", "0",
-                        "--repeat", "1"], capture_output=True, text=True, timeout=900)
+                        "--repeat", "1"], capture_output=True, text=True, timeout=900, env=env)
     lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{\"products\"")]
     info = json.loads(lines[-1]) if lines else {"error": r.stderr.strip().splitlines()[-3:]}
+    te = total_est(r.stderr)
+    if te is not None:
+        info["total_est"] = te
     if r.returncode != 0 or not out.exists():
         return None, info
     return M.load_bin(out), info
@@ -89,10 +123,27 @@ def digest(C: M.Csr, rng) -> dict:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--out", default="gpurun_out/golden")
+    ap.add_argument("--out", default=str(ROOT / "tests" / "golden"))
+    ap.add_argument("--estimates", action="store_true",
+                    help="only the estimator pins (writes estimates.json)")
     a = ap.parse_args()
     out = Path(a.out)
     out.mkdir(parents=True, exist_ok=True)
+    if a.estimates:
+        est = {}
+        with tempfile.TemporaryDirectory() as tdn:
+            td = Path(tdn)
+            for case, (g, kw, meth) in ESTIMATES.items():
+                A = gen(g, kw)
+                _, info = run_ref(meth, A, td)
+                _, info_hll = run_ref(meth, A, td, est_method="hll")
+                est[case] = {"generator": g, "kwargs": kw, "method": meth, "nnz_a": A.nnz,
+                             "total_est": info.get("total_est"),
+                             "total_est_hll": info_hll.get("total_est"),
+                             "c_nnz": info.get("c_nnz"), "products": info.get("products")}
+                print(case, est[case], flush=True)
+        (out / "estimates.json").write_text(json.dumps(est, indent=1))
+        return 0
     manifest = {}
     with tempfile.TemporaryDirectory() as tdn:
         td = Path(tdn)

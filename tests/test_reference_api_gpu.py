@@ -1,5 +1,6 @@
 """The reference-compatible entry points (include/spgemm.h names and layouts) through the C ABI."""
 import ctypes as ct
+import re
 
 import numpy as np
 import pytest
@@ -93,3 +94,39 @@ def test_device_resident_row_block_upper():
     assert np.array_equal(crp, full.row_ptr[r0:r1 + 1] - lo)
     assert np.array_equal(cci, full.col_idx[lo:hi])
     assert np.allclose(cva, full.val[lo:hi], rtol=1e-12, atol=1e-14)
+
+
+def _compute_only_from_prof(stderr: str, tag: str):
+    """The reference's compute-only rule over HashProf lines (scripts/compare_methods.py:37-52,
+    restated): phases by name from "[<tag>] <phase> <ms> ms", then TOTAL(GPU) - h2d - d2h."""
+    rx = re.compile(r"\[" + re.escape(tag) + r"\]\s+(\S+)\s+([0-9.]+)\s+ms")
+    phases = {}
+    for line in stderr.splitlines():
+        m = rx.search(line)
+        if m:
+            phases[m.group(1)] = float(m.group(2))
+    if not phases or "TOTAL(GPU)" not in phases:
+        return None, phases
+    return phases["TOTAL(GPU)"] - phases.get("h2d", 0.0) - phases.get("d2h", 0.0), phases
+
+
+@pytest.mark.parametrize("entry,tag", [("spgemm_self_product_adaptive", "hash-prof"),
+                                       ("spgemm_self_product_hash", "hash-prof"),
+                                       ("spgemm_self_product_merge3", "mrg3-prof")])
+def test_phase_profile_parses_like_the_reference(entry, tag, monkeypatch, capfd):
+    """With APPT_PROF=1 the reference entry points print per-phase device times in the
+    reference's HashProf format (include/hash_prof.h:9-28) under the tag its scripts look for,
+    and the adaptive entry prints its choice line on stdout (src/spgemm_adaptive.cu:85)."""
+    monkeypatch.setenv("APPT_PROF", "1")
+    A = M.stencil27(g=24)
+    C, _, _, cn = ap.reference_entry(entry, A)
+    assert cn > 0
+    out, err = capfd.readouterr()
+    comp, phases = _compute_only_from_prof(err, tag)
+    assert comp is not None, err
+    assert 0.0 < comp <= phases["TOTAL(GPU)"]
+    known = {"h2d", "transpose", "analyze", "symbolic", "scan", "numeric", "d2h", "other"}
+    assert set(phases) - {"TOTAL(GPU)"} <= known, phases
+    if entry == "spgemm_self_product_adaptive":
+        adapt = " ".join(ln for ln in out.splitlines() if "[adapt]" in ln)
+        assert re.findall(r"→\s*(hash|merge3)", adapt)[-1] == "hash", out
