@@ -24,7 +24,9 @@ import numpy as np
 from .matrices import Csr
 
 PKG_DIR = Path(__file__).resolve().parent.parent
-LIB_PATH = PKG_DIR / "libappt_spgemm.so"
+# APPT_LIB selects another build of the library (e.g. a variant built with build.py)
+LIB_PATH = Path(os.environ["APPT_LIB"]) if os.environ.get("APPT_LIB") else \
+    PKG_DIR / "libappt_spgemm.so"
 
 OPS = {"ab": 0, "aat": 1, "aat_upper": 2, "ab_upper": 3}
 METHODS = {"adaptive": 0, "hash": 1, "merge": 2, "esc": 3}

@@ -18,8 +18,11 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
-BUILD = PKG / "_build"
-LIB = PKG / "libappt_spgemm.so"
+# A build variant (APPT_BUILD_VARIANT=<name>, with its own APPT_NVCC_DEFINES) goes to
+# _build/<name>/ and _build/<name>/libappt_spgemm.so; load it with APPT_LIB=<that path>.
+VARIANT = os.environ.get("APPT_BUILD_VARIANT", "")
+BUILD = PKG / "_build" / VARIANT if VARIANT else PKG / "_build"
+LIB = BUILD / "libappt_spgemm.so" if VARIANT else PKG / "libappt_spgemm.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=default",
@@ -51,7 +54,7 @@ def _compile(src: Path, verbose: bool, ptxas_info: bool) -> tuple[Path, str]:
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
-    BUILD.mkdir(exist_ok=True)
+    BUILD.mkdir(parents=True, exist_ok=True)
     hdr = _headers_mtime()
     stamp = BUILD / "flags.txt"
     flags = " ".join(ARCH + COMMON)

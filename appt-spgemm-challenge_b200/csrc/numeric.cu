@@ -129,6 +129,34 @@ __global__ void __launch_bounds__(WPB * 32, 2048 / (WPB * 32) * 3 / 4) num_warp_
 #ifndef APPT_RANK_MIN_BLOCKS
 #define APPT_RANK_MIN_BLOCKS 4  // resident 256-thread CTAs per SM the register budget targets
 #endif
+// Depth of the cp.async ring that stages B entries for one-group rows (0: loads into registers,
+// two steps ahead).
+#ifndef APPT_RANK_STAGE
+#define APPT_RANK_STAGE 0
+#endif
+template <int G>
+__host__ __device__ constexpr int rank_ring_bytes() {
+  return (APPT_RANK_STAGE > 1 && G == 1) ? 12 * 32 * APPT_RANK_STAGE : 0;
+}
+
+// One chunk of A entries of a rank-tier row (see accumulate_chunk_ranked).
+template <int G>
+__device__ __forceinline__ void rank_chunk(const Csr& B, int bs, int len, double a, int cnt,
+                                           int lo, unsigned span, int n, const unsigned* bm,
+                                           const unsigned short* pre, double* acc,
+                                           unsigned short* coff, unsigned char* ring) {
+#if APPT_RANK_STAGE > 1
+  if (G == 1 && !__any_sync(kFull, len > 32)) {
+    accumulate_chunk_ranked_staged<APPT_RANK_STAGE>(
+        B, bs, len, a, cnt, lo, span, n, bm, pre, acc, coff, reinterpret_cast<int*>(ring),
+        reinterpret_cast<double*>(ring + 128 * APPT_RANK_STAGE));
+    return;
+  }
+#endif
+  (void)ring;
+  accumulate_chunk_ranked<G>(B, bs, len, a, cnt, lo, span, n, bm, pre, acc, coff);
+}
+
 template <int BUDGET, int WPB, int G>
 __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCKS : 7)
     num_warp_rank_kernel(
@@ -137,7 +165,8 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     double* cval, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  unsigned char* base = num_smem + (size_t)warp * BUDGET;
+  unsigned char* base = num_smem + (size_t)warp * (BUDGET + rank_ring_bytes<G>());
+  unsigned char* ring = base + BUDGET;
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
   for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
@@ -192,13 +221,11 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     if (running != n) bad = true;
     // 3) accumulate at the column's rank, k by k; remember the column of every rank
     if (running == n) {
-      accumulate_chunk_ranked<G>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre, acc,
-                                       coff);
+      rank_chunk<G>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre, acc, coff, ring);
       for (int cb = rs + 32; cb < re; cb += 32) {
         load_chunk(A, B, cb, re, bs, len, &a);
         const int c2 = (re - cb) < 32 ? (re - cb) : 32;
-        accumulate_chunk_ranked<G>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre, acc,
-                                         coff);
+        rank_chunk<G>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre, acc, coff, ring);
       }
       // 4) the row is already in column order: one coalesced copy
       for (int t = lane; t < n; t += 32) {
@@ -687,7 +714,7 @@ void run_warp_rank_g(int bin, const int* rows, const long long* bin_off, long lo
                      Csr B, int upper, int row_base, const int* lo, const int* hi,
                      const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
                      double* cval, int* err, int num_sms, cudaStream_t s) {
-  const size_t smem = (size_t)WPB * BUDGET;
+  const size_t smem = (size_t)WPB * (BUDGET + rank_ring_bytes<G>());
   auto kern = num_warp_rank_kernel<BUDGET, WPB, G>;
   smem_opt_in((const void*)kern, smem);
   const int grid = occupancy_grid(kern, WPB * 32, smem, num_sms, nrows, WPB);

@@ -141,10 +141,9 @@ __host__ __device__ __forceinline__ int bitmap_words(long long span) {
 // Presence bitmap of the row's columns: bit (j - lo) of logical word (j - lo) / 32 is set for
 // every product column j (order-free). The chunk's B row bounds are passed in (one A entry per lane). In the
 // common case the column indices of kFillBatch consecutive steps are loaded before any of them
-// is applied, so that many loads are in flight per warp; a batch that runs past the chunk wraps
-// to entries of the same chunk, which set bits that are set anyway. Returns true if a column
-// lies above the span (B rows not sorted); columns below lo are skipped (they are the ones the
-// upper-triangle variants drop).
+// is applied, so that many loads are in flight per warp; the last batch of a chunk stops at the
+// chunk's end (a warp-uniform exit). Returns true if a column lies above the span (B rows not
+// sorted); columns below lo are skipped (they are the ones the upper-triangle variants drop).
 constexpr int kFillBatch = 8;
 
 template <int G>
@@ -159,12 +158,14 @@ __device__ __forceinline__ bool fill_chunk_bitmap(const Csr& B, int bs, int len,
       int jj[kFillBatch];
 #pragma unroll
       for (int u = 0; u < kFillBatch; ++u) {
+        if (t0 + u * G >= cnt) break;   // uniform: the chunk ends inside this batch
         const int t = (t0 + u * G + grp) & 31;
         jj[u] = load_b_entry(B, __shfl_sync(kFull, bs, t), __shfl_sync(kFull, len, t), sub, lo,
                              nullptr);
       }
 #pragma unroll
       for (int u = 0; u < kFillBatch; ++u) {
+        if (t0 + u * G >= cnt) break;
         const unsigned off = (unsigned)(jj[u] - lo);
         red_or_shared_if(off < span, bm + swz(off >> 5), 1u << (off & 31));
         bad |= jj[u] > hi;
@@ -326,6 +327,67 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
       }
     }
   }
+}
+
+// Variant of accumulate_chunk_ranked for one lane group (G = 1) whose B entries are staged
+// through a per-warp ring of D steps in shared memory with cp.async (LDGSTS): each lane copies
+// its own entry of the step D - 1 ahead (column 4 B, value 8 B; a lane without an entry copies
+// nothing and zero-fills), and reads back only what it copied itself, so the ring needs no warp
+// barrier. The entries of D - 1 steps are in flight without occupying registers.
+// ring: D * 32 ints followed by D * 32 doubles (12 * 32 * D bytes, 8-byte aligned).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool full) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src),
+               "r"(full ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src, bool full) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(src),
+               "r"(full ? 8 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+template <int D>
+__device__ __forceinline__ void accumulate_chunk_ranked_staged(
+    const Csr& B, int bs, int len, double a, int cnt, int lo, unsigned span, int n,
+    const unsigned* bm, const unsigned short* pre, double* acc, unsigned short* coff,
+    int* ring_ci, double* ring_val) {
+  const int lane = threadIdx.x & 31;
+  // issue the copies of step t into slot t % D (a step past the chunk copies nothing)
+  auto issue = [&](int t) {
+    const int tt = t & 31;
+    const int bt = __shfl_sync(kFull, bs, tt);
+    const int lt = __shfl_sync(kFull, len, tt);
+    const bool v = t < cnt && lane < lt;
+    const int idx = v ? bt + lane : 0;
+    const int slot = (t % D) * 32 + lane;
+    cp_async4(ring_ci + slot, B.ci + idx, v);
+    cp_async8(ring_val + slot, B.val + idx, v);
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int t = 0; t < D - 1; ++t) issue(t);
+  for (int t = 0; t < cnt; ++t) {
+    issue(t + D - 1);
+    cp_async_wait<D - 1>();   // step t's group has landed (this lane's own copies)
+    const int slot = (t % D) * 32 + lane;
+    const int lt = __shfl_sync(kFull, len, t);
+    const int j = lane < lt ? ring_ci[slot] : lo - 1;
+    const double x = ring_val[slot];
+    const unsigned off = (unsigned)(j - lo);
+    const int r = rank_or(bm, pre, off, span, n);
+    const double at = __shfl_sync(kFull, a, t);
+    acc[r] = __dadd_rn(acc[r], __dmul_rn(at, x));
+    coff[r] = (unsigned short)off;
+    __syncwarp();
+  }
+  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------------------------

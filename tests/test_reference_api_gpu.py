@@ -130,3 +130,53 @@ def test_phase_profile_parses_like_the_reference(entry, tag, monkeypatch, capfd)
     if entry == "spgemm_self_product_adaptive":
         adapt = " ".join(ln for ln in out.splitlines() if "[adapt]" in ln)
         assert re.findall(r"→\s*(hash|merge3)", adapt)[-1] == "hash", out
+
+
+def _driver():
+    drv = ap.PKG_DIR / "_build" / "spgemm_test"
+    if not drv.exists():
+        pytest.skip("reference driver not built (reference sources absent at build time)")
+    return drv
+
+
+@pytest.mark.parametrize("fmt", ["bin", "mtx"])
+def test_reference_driver_runs_on_the_library(tmp_path, fmt):
+    """The reference's own src/main.cu, linked against this library (no reference kernels), run
+    the way the reference's scripts run it (USE_MEMPOOL=1, METHOD=...): every method's nnz(C)
+    equals the oracle's, and its adaptive output parses like the reference's
+    (scripts/compare_methods.py: "[adapt] ... -> hash", HashProf lines, "Result C" / "Time")."""
+    import os
+    import subprocess
+    drv = _driver()
+    A = M.stencil27(g=20)
+    path = tmp_path / f"a.{fmt}"
+    if fmt == "bin":
+        M.save_bin(path, A)
+    else:   # text with full-precision values, entries row by row
+        rows = np.repeat(np.arange(A.rows), np.diff(A.row_ptr))
+        body = "\n".join(f"{r + 1} {c + 1} {v!r}" for r, c, v in
+                         zip(rows.tolist(), A.col_idx.tolist(), A.val.tolist()))
+        path.write_text(f"%%MatrixMarket matrix coordinate real general\n{A.rows} {A.cols} "
+                        f"{A.nnz}\n{body}\n")
+    want = oracle.spgemm(A).nnz
+    want_upper = oracle.spgemm(A, op="aat_upper").nnz
+    for method in ("adaptive", "hash", "merge3", "manual"):
+        env = dict(os.environ, USE_MEMPOOL="1", METHOD=method, APPT_PROF="1")
+        r = subprocess.run([str(drv), str(path)], capture_output=True, text=True, cwd=tmp_path,
+                           env=env, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        nz = re.findall(r"Result C:.*?nnz\s*=\s*(\d+)", r.stdout)
+        assert nz and int(nz[-1]) == want, r.stdout[-2000:]
+        assert re.search(r"Time:\s*([0-9.]+)\s*ms", r.stdout)
+        if method == "adaptive":
+            adapt = " ".join(ln for ln in r.stdout.splitlines() if "[adapt]" in ln)
+            assert re.findall(r"→\s*(hash|merge3)", adapt)[-1] == "hash"
+            comp, _ = _compute_only_from_prof(r.stderr, "hash-prof")
+            assert comp is not None and comp > 0
+    env = dict(os.environ, USE_MEMPOOL="1", METHOD="all")
+    r = subprocess.run([str(drv), str(path), "att"], capture_output=True, text=True, cwd=tmp_path,
+                       env=env, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    nz = [int(x) for x in re.findall(r"Result C \(.*?\):.*?nnz\s*=\s*(\d+)", r.stdout)]
+    assert len(nz) == 4 and nz[0] == oracle.spgemm(A, op="aat").nnz, r.stdout[-2000:]
+    assert nz[1:] == [want_upper] * 3
