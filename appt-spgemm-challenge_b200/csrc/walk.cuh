@@ -141,9 +141,11 @@ __host__ __device__ __forceinline__ int bitmap_words(long long span) {
 // Presence bitmap of the row's columns: bit (j - lo) of logical word (j - lo) / 32 is set for
 // every product column j (order-free). The chunk's B row bounds are passed in (one A entry per lane). In the
 // common case the column indices of kFillBatch consecutive steps are loaded before any of them
-// is applied, so that many loads are in flight per warp; the last batch of a chunk stops at the
-// chunk's end (a warp-uniform exit). Returns true if a column lies above the span (B rows not
-// sorted); columns below lo are skipped (they are the ones the upper-triangle variants drop).
+// is applied, so that many loads are in flight per warp; a batch that runs past the chunk wraps
+// to entries of the same chunk, which set bits that are set anyway (stopping the last batch at
+// the chunk's end measured slower: the early exits break up the batched loads). Returns true if
+// a column lies above the span (B rows not sorted); columns below lo are skipped (they are the
+// ones the upper-triangle variants drop).
 constexpr int kFillBatch = 8;
 
 template <int G>
@@ -158,14 +160,12 @@ __device__ __forceinline__ bool fill_chunk_bitmap(const Csr& B, int bs, int len,
       int jj[kFillBatch];
 #pragma unroll
       for (int u = 0; u < kFillBatch; ++u) {
-        if (t0 + u * G >= cnt) break;   // uniform: the chunk ends inside this batch
         const int t = (t0 + u * G + grp) & 31;
         jj[u] = load_b_entry(B, __shfl_sync(kFull, bs, t), __shfl_sync(kFull, len, t), sub, lo,
                              nullptr);
       }
 #pragma unroll
       for (int u = 0; u < kFillBatch; ++u) {
-        if (t0 + u * G >= cnt) break;
         const unsigned off = (unsigned)(jj[u] - lo);
         red_or_shared_if(off < span, bm + swz(off >> 5), 1u << (off & 31));
         bad |= jj[u] > hi;

@@ -55,14 +55,16 @@ SMALL = {
     "banded_n4096": ("banded", {"n": 4096}, ["adaptive", "hash", "merge3"]),
     "rmat_s10": ("rmat", {"scale": 10}, ["adaptive", "hash", "merge3", "att_adaptive"]),
 }
-# Estimator pins: (generator, kwargs, reference method). All have >= 100000 nonzeros.
+# Estimator pins: (generator, kwargs, reference method). All have >= 100000 nonzeros, and on
+# each the oracle's restatement of both estimators never sizes a row below its exact nnz (the
+# reference writes a row's entries at its estimate-sized slot, so an underestimate would spill
+# into the next row's slot; R-MAT inputs do underestimate some rows and are left out).
 ESTIMATES = {
     "stencil27_g24": ("stencil27", {"g": 24}, "hash"),
     "stencil27_g40": ("stencil27", {"g": 40}, "hash"),
     "stencil27_g64": ("stencil27", {}, "hash"),
     "uniform8_n32768": ("uniform8", {"n": 32768}, "hash"),
     "banded_n32768": ("banded", {"n": 32768}, "hash"),
-    "rmat_s14": ("rmat", {"scale": 14}, "hash"),
     "random_3000": ("random_csr", {"rows": 3000, "cols": 3000, "density": 0.02, "seed": 31},
                     "hash"),
     "stencil27_g24_att": ("stencil27", {"g": 24}, "att_hash"),
