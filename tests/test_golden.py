@@ -111,3 +111,42 @@ def test_engine_matches_reference(key, ent):
         check_full(C, np.load(GOLDEN / ent["file"]), _scale(A, op))
     else:
         check_digest(C, json.loads((GOLDEN / ent["file"]).read_text()), _scale(A, op))
+
+
+# ----------------------------------------------------------------------------- estimator pins
+ESTIMATES = GOLDEN / "estimates.json"
+
+
+def _est_cases():
+    if not ESTIMATES.exists():
+        return []
+    est = json.loads(ESTIMATES.read_text())
+    return [pytest.param(k, e, id=k) for k, e in sorted(est.items())]
+
+
+@pytest.mark.parametrize("key,ent", _est_cases())
+def test_oracle_estimate_matches_reference_total(key, ent):
+    """The oracle's restatement of the reference's MinHash and HyperLogLog sizing estimates sums
+    to the reference's own "[hash] total_est" (src/spgemm_kernel_hash.cu:925), recorded by
+    tests/golden/make_golden.py --estimates from the reference's CUDA build."""
+    A = _input(ent)
+    att = ent["method"].startswith("att")
+    mh = oracle.estimate_row_nnz(A, att=att, estimator="minhash").astype(np.int64)
+    hll = oracle.estimate_row_nnz(A, att=att, estimator="hll").astype(np.int64)
+    assert int(mh.sum()) == ent["total_est"]
+    assert int(hll.sum()) == ent["total_est_hll"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("key,ent", _est_cases())
+def test_engine_estimate_matches_reference_total(key, ent):
+    """The engine's estimator (appt_estimate_row_nnz) sums to the reference's total_est and
+    agrees row by row with the oracle's restatement."""
+    import appt_spgemm as ap
+    A = _input(ent)
+    att = ent["method"].startswith("att")
+    for name, key_total in (("minhash", "total_est"), ("hll", "total_est_hll")):
+        e = ap.estimate_row_nnz(A, att=att, estimator=name).astype(np.int64)
+        assert int(e.sum()) == ent[key_total], name
+        r = oracle.estimate_row_nnz(A, att=att, estimator=name).astype(np.int64)
+        assert np.array_equal(e, r), (name, int((e != r).sum()))
