@@ -129,34 +129,6 @@ __global__ void __launch_bounds__(WPB * 32, 2048 / (WPB * 32) * 3 / 4) num_warp_
 #ifndef APPT_RANK_MIN_BLOCKS
 #define APPT_RANK_MIN_BLOCKS 4  // resident 256-thread CTAs per SM the register budget targets
 #endif
-// Depth of the cp.async ring that stages B entries for one-group rows (0: loads into registers,
-// two steps ahead).
-#ifndef APPT_RANK_STAGE
-#define APPT_RANK_STAGE 0
-#endif
-template <int G>
-__host__ __device__ constexpr int rank_ring_bytes() {
-  return (APPT_RANK_STAGE > 1 && G == 1) ? 12 * 32 * APPT_RANK_STAGE : 0;
-}
-
-// One chunk of A entries of a rank-tier row (see accumulate_chunk_ranked).
-template <int G>
-__device__ __forceinline__ void rank_chunk(const Csr& B, int bs, int len, double a, int cnt,
-                                           int lo, unsigned span, int n, const unsigned* bm,
-                                           const unsigned short* pre, double* acc,
-                                           unsigned short* coff, unsigned char* ring) {
-#if APPT_RANK_STAGE > 1
-  if (G == 1 && !__any_sync(kFull, len > 32)) {
-    accumulate_chunk_ranked_staged<APPT_RANK_STAGE>(
-        B, bs, len, a, cnt, lo, span, n, bm, pre, acc, coff, reinterpret_cast<int*>(ring),
-        reinterpret_cast<double*>(ring + 128 * APPT_RANK_STAGE));
-    return;
-  }
-#endif
-  (void)ring;
-  accumulate_chunk_ranked<G>(B, bs, len, a, cnt, lo, span, n, bm, pre, acc, coff);
-}
-
 template <int BUDGET, int WPB, int G>
 __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCKS : 7)
     num_warp_rank_kernel(
@@ -165,8 +137,7 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     double* cval, int* err) {
   extern __shared__ __align__(16) unsigned char num_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  unsigned char* base = num_smem + (size_t)warp * (BUDGET + rank_ring_bytes<G>());
-  unsigned char* ring = base + BUDGET;
+  unsigned char* base = num_smem + (size_t)warp * BUDGET;
   const long long b0 = bin_off[bin];
   const long long nrows = bin_off[bin + 1] - b0;
   for (long long r = (long long)blockIdx.x * WPB + warp; r < nrows;
@@ -192,11 +163,10 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     unsigned short* pre = reinterpret_cast<unsigned short*>(base + 4 * W);
     double* acc = reinterpret_cast<double*>(base + acc_off);              // n sums + spare
     unsigned short* coff = reinterpret_cast<unsigned short*>(base + acc_off + 8 * (n + 1));
-    const unsigned* hbm = nullptr;   // the symbolic phase's bitmap of this row, if handed off
-    if (handoff.data) {
-      const int hs = handoff.slot[i];
-      if (hs >= 0) hbm = handoff.data + 32ll * hs;
-    }
+    // the symbolic phase's record of this row's columns, if it handed one off
+    const int hs = handoff.data ? handoff.slot[i] : -1;
+    const bool has_list = hs >= 0 && (hs & kHandoffList);
+    const unsigned* hrec = hs >= 0 ? handoff.data + (hs & (kHandoffList - 1)) : nullptr;
     for (int t = lane; t < n; t += 32) acc[t] = 0.0;
     // the first chunk of A entries stays in registers
     int bs, len;
@@ -204,9 +174,21 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     load_chunk(A, B, rs, re, bs, len, &a);
     const int cnt = (re - rs) < 32 ? (re - rs) : 32;
     bool bad = false;
-    // 1) presence bitmap of the row's columns: copied in, or built from the products
-    if (hbm) {
-      for (int w = lane; w < W; w += 32) bm[swz(w)] = __ldg(hbm + w);
+    // 1) presence bitmap of the row's columns: from the handed-off column list (which also
+    //    gives C's columns in order), copied in, or built from the products
+    if (has_list) {
+      for (int w = lane; w < W; w += 32) bm[w] = 0u;
+      __syncwarp();
+      const unsigned short* lst = reinterpret_cast<const unsigned short*>(hrec);
+      for (int t = lane; t < n; t += 32) {
+        const unsigned off = __ldg(lst + t);
+        coff[t] = (unsigned short)off;
+        bad |= off >= (unsigned)span;
+        red_or_shared_if(off < (unsigned)span, bm + swz(off >> 5), 1u << (off & 31));
+      }
+      __syncwarp();
+    } else if (hrec) {
+      for (int w = lane; w < W; w += 32) bm[swz(w)] = __ldg(hrec + w);
       __syncwarp();
     } else {
       for (int w = lane; w < W; w += 32) bm[w] = 0u;
@@ -219,13 +201,27 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     const int running = bitmap_prefix32(bm, W, pre);
     __syncwarp();
     if (running != n) bad = true;
-    // 3) accumulate at the column's rank, k by k; remember the column of every rank
+    // 3) accumulate at the column's rank, k by k; remember the column of every rank (unless the
+    //    list gave them)
     if (running == n) {
-      rank_chunk<G>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre, acc, coff, ring);
-      for (int cb = rs + 32; cb < re; cb += 32) {
-        load_chunk(A, B, cb, re, bs, len, &a);
-        const int c2 = (re - cb) < 32 ? (re - cb) : 32;
-        rank_chunk<G>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre, acc, coff, ring);
+      if (has_list) {
+        accumulate_chunk_ranked<G, false>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre,
+                                          acc, coff);
+        for (int cb = rs + 32; cb < re; cb += 32) {
+          load_chunk(A, B, cb, re, bs, len, &a);
+          const int c2 = (re - cb) < 32 ? (re - cb) : 32;
+          accumulate_chunk_ranked<G, false>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre,
+                                            acc, coff);
+        }
+      } else {
+        accumulate_chunk_ranked<G>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre, acc,
+                                   coff);
+        for (int cb = rs + 32; cb < re; cb += 32) {
+          load_chunk(A, B, cb, re, bs, len, &a);
+          const int c2 = (re - cb) < 32 ? (re - cb) : 32;
+          accumulate_chunk_ranked<G>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre, acc,
+                                     coff);
+        }
       }
       // 4) the row is already in column order: one coalesced copy
       for (int t = lane; t < n; t += 32) {
@@ -714,7 +710,7 @@ void run_warp_rank_g(int bin, const int* rows, const long long* bin_off, long lo
                      Csr B, int upper, int row_base, const int* lo, const int* hi,
                      const long long* flop, RowBitmaps handoff, const long long* crp, int* cci,
                      double* cval, int* err, int num_sms, cudaStream_t s) {
-  const size_t smem = (size_t)WPB * (BUDGET + rank_ring_bytes<G>());
+  const size_t smem = (size_t)WPB * BUDGET;
   auto kern = num_warp_rank_kernel<BUDGET, WPB, G>;
   smem_opt_in((const void*)kern, smem);
   const int grid = occupancy_grid(kern, WPB * 32, smem, num_sms, nrows, WPB);

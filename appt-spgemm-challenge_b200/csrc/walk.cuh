@@ -230,12 +230,13 @@ __device__ __forceinline__ int rank_or(const unsigned* bm, const unsigned short*
   return ok ? min(r, dummy) : dummy;
 }
 
-// Ranked accumulation over one chunk of A entries: acc[rank(j)] += a_ik * b_kj and
+// Ranked accumulation over one chunk of A entries: acc[rank(j)] += a_ik * b_kj and, with COFF,
 // coff[rank(j)] = j - lo for every product with j in the span, k-sequentially (G ordered
-// sub-phases per step when G > 1). Lanes without a product in a (sub-)phase update the
-// spare slot acc[n] / coff[n] instead, so the step has no branch. In the common case the B
-// entries of the next two steps are loaded while the current step is applied.
-template <int G>
+// sub-phases per step when G > 1); without COFF the columns of the ranks are already known (a
+// handed-off column list). Lanes without a product in a (sub-)phase update the spare slot
+// acc[n] / coff[n] instead, so the step has no branch. In the common case the B entries of the
+// next two steps are loaded while the current step is applied.
+template <int G, bool COFF = true>
 __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, int len, double a,
                                                         int cnt, int lo, unsigned span, int n,
                                                         const unsigned* bm,
@@ -271,7 +272,7 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
       for (int g = 0; g < G; ++g) {
         const int pos = (G == 1 || grp == g) ? r0 : n;
         acc[pos] = __dadd_rn(acc[pos], p0);
-        coff[pos] = (unsigned short)off0;
+        if (COFF) coff[pos] = (unsigned short)off0;
         __syncwarp();
       }
       off0 = off1;
@@ -298,7 +299,7 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
       for (int g = 0; g < G; ++g) {
         const int pos = (G == 1 || grp == g) ? r0 : n;
         acc[pos] = __dadd_rn(acc[pos], p0);
-        coff[pos] = (unsigned short)off0;
+        if (COFF) coff[pos] = (unsigned short)off0;
         __syncwarp();
       }
       off0 = (unsigned)(j1 - lo);
@@ -320,74 +321,13 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
             const unsigned off = (unsigned)(j - lo);
             const int pos = rank_or(bm, pre, off, span, n);
             acc[pos] = mul_add_rn(acc[pos], at, __ldg(B.val + bt + q));
-            coff[pos] = (unsigned short)off;
+            if (COFF) coff[pos] = (unsigned short)off;
           }
         }
         __syncwarp();
       }
     }
   }
-}
-
-// Variant of accumulate_chunk_ranked for one lane group (G = 1) whose B entries are staged
-// through a per-warp ring of D steps in shared memory with cp.async (LDGSTS): each lane copies
-// its own entry of the step D - 1 ahead (column 4 B, value 8 B; a lane without an entry copies
-// nothing and zero-fills), and reads back only what it copied itself, so the ring needs no warp
-// barrier. The entries of D - 1 steps are in flight without occupying registers.
-// ring: D * 32 ints followed by D * 32 doubles (12 * 32 * D bytes, 8-byte aligned).
-__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool full) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src),
-               "r"(full ? 4 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async8(void* dst, const void* src, bool full) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(src),
-               "r"(full ? 8 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
-template <int D>
-__device__ __forceinline__ void accumulate_chunk_ranked_staged(
-    const Csr& B, int bs, int len, double a, int cnt, int lo, unsigned span, int n,
-    const unsigned* bm, const unsigned short* pre, double* acc, unsigned short* coff,
-    int* ring_ci, double* ring_val) {
-  const int lane = threadIdx.x & 31;
-  // issue the copies of step t into slot t % D (a step past the chunk copies nothing)
-  auto issue = [&](int t) {
-    const int tt = t & 31;
-    const int bt = __shfl_sync(kFull, bs, tt);
-    const int lt = __shfl_sync(kFull, len, tt);
-    const bool v = t < cnt && lane < lt;
-    const int idx = v ? bt + lane : 0;
-    const int slot = (t % D) * 32 + lane;
-    cp_async4(ring_ci + slot, B.ci + idx, v);
-    cp_async8(ring_val + slot, B.val + idx, v);
-    cp_async_commit();
-  };
-#pragma unroll
-  for (int t = 0; t < D - 1; ++t) issue(t);
-  for (int t = 0; t < cnt; ++t) {
-    issue(t + D - 1);
-    cp_async_wait<D - 1>();   // step t's group has landed (this lane's own copies)
-    const int slot = (t % D) * 32 + lane;
-    const int lt = __shfl_sync(kFull, len, t);
-    const int j = lane < lt ? ring_ci[slot] : lo - 1;
-    const double x = ring_val[slot];
-    const unsigned off = (unsigned)(j - lo);
-    const int r = rank_or(bm, pre, off, span, n);
-    const double at = __shfl_sync(kFull, a, t);
-    acc[r] = __dadd_rn(acc[r], __dmul_rn(at, x));
-    coff[r] = (unsigned short)off;
-    __syncwarp();
-  }
-  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -96,15 +96,13 @@ def parse_args():
     return ap.parse_args()
 
 
-def config_of(wl, A, c_nnz, products, method, world, extra=None) -> dict:
-    """The `config` object both arms print (same keys, so the lines compare like for like)."""
-    cfg = {"workload": wl["name"], "rows": A.rows, "cols": A.cols, "nnz_a": A.nnz,
-           "nnz_c": int(c_nnz), "products": int(products), "method": method,
-           "parallelism": f"row-sharded x{world}" if world > 1 else "one GPU",
-           "l2": "flushed between steps (256 MB write)"}
-    if extra:
-        cfg.update(extra)
-    return cfg
+def config_of(wl, A, c_nnz, products, method, world) -> dict:
+    """The `config` object both arms print: the same keys and, for the same workload on one GPU,
+    the same values, so the lines compare like for like (how each arm was run is in top-level
+    keys)."""
+    return {"workload": wl["name"], "rows": A.rows, "cols": A.cols, "nnz_a": A.nnz,
+            "nnz_c": int(c_nnz), "products": int(products), "method": method,
+            "parallelism": f"row-sharded x{world}" if world > 1 else "one GPU"}
 
 
 # ----------------------------------------------------------------------------- helpers
@@ -326,9 +324,9 @@ def run_reference(args, rank: int, world: int):
     line = {**base, "value": val, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f64", "data": f"synthetic ({wl['data']})",
-            "config": config_of(wl, A, cn, P, args.method, 1,
-                                {"reference": "oracle/_ref/ref_spgemm (unmodified reference "
-                                              "sources, sm_100a, USE_MEMPOOL=1)"}),
+            "config": config_of(wl, A, cn, P, args.method, 1),
+            "reference_build": "oracle/_ref/ref_spgemm (unmodified reference sources, sm_100a, "
+                               "USE_MEMPOOL=1)",
             "value_rule": rule,
             "clocks": clocks,
             "cpu_baseline": {"value": val, "unit": UNIT, "cores": 1, "kind": "reference",
@@ -617,9 +615,9 @@ def main():
             "warmup": args.warmup, "ms_per_step": t_total_max / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
             "data": f"synthetic ({wl['data']})",
-            "config": config_of(wl, A, all_cnnz, all_products, args.method, world,
-                                {"row_blocks_per_rank": len(blocks) - 1,
-                                 "b_replication_ms": t_rep}),
+            "config": config_of(wl, A, all_cnnz, all_products, args.method, world),
+            "l2": "flushed between steps (256 MB write)",
+            "row_blocks_per_rank": len(blocks) - 1, "b_replication_ms": t_rep,
             "effective_gbs": cbytes / (t_total_max / args.steps * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": tr,
