@@ -18,16 +18,13 @@ constexpr int kSymBlockWords = 32768;   // CTA symbolic bitmap window: 2^20 colu
 constexpr int kMergeMaxLists = 256;     // merge tier: rows with more A entries use other tiers
 constexpr int kRankMaxBudget = 9216;    // largest per-warp shared budget of the rank tier (bytes)
 
-// The column set of a row that the symbolic bitmap tier hands to the rank tier of the numeric
-// phase, so that the numeric phase need not walk the row's products twice. A record is the
-// cheaper of two forms: the row's span bitmap (W words, logical word order), or -- when it is
-// smaller -- the row's sorted column offsets j - lo as 16-bit values (n entries, padded to
-// whole words), which also are the columns of C's row in output order. Records live in one
-// arena of `capacity` words; each warp of the symbolic kernel takes chunks of it with one atomic
-// on `top`. slot[i] = word offset of row i's record, with kHandoffList set for the list form,
-// or -1 (no record: the arena was full, the row does not qualify, or it ran in another tier).
-// Only rows that could fit the rank tier get a record, and a bitmap only when the products
-// outweigh it (handoff_pays). data == nullptr: no handoff at all.
+// Column bitmaps that the symbolic bitmap tier hands to the rank tier of the numeric phase, so
+// that the numeric phase need not walk the products twice. The bitmaps live in one arena of
+// `capacity` words; each warp of the symbolic kernel takes chunks of it with one atomic on `top`
+// and places its rows' bitmaps there (logical word order). slot[i] = first word of row i's bitmap
+// / 32, or -1 (no bitmap: the arena was full, the row does not qualify, or it ran in another
+// tier). Only rows that could fit the rank tier and whose products outweigh their bitmap
+// (handoff_pays) are handed off. data == nullptr: no handoff at all.
 struct RowBitmaps {
   int* slot = nullptr;
   unsigned* data = nullptr;
@@ -35,21 +32,17 @@ struct RowBitmaps {
   long long capacity = 0;
 };
 
-constexpr int kHandoffList = 1 << 30;               // slot flag: the record is a column list
 constexpr int kHandoffChunkWords = 16384;          // arena words a warp takes at a time
-constexpr long long kHandoffArenaWords = 1ll << 28;  // arena size (1 GiB; offsets < 2^30)
+constexpr long long kHandoffArenaWords = 1ll << 28;  // arena size (1 GiB)
 
 __host__ __device__ __forceinline__ bool handoff_fits_rank(int bitmap_words) {
   return 6ll * bitmap_words + 20 <= kRankMaxBudget;
 }
 
-// Words of a row's column list (n 16-bit offsets).
-__host__ __device__ __forceinline__ int handoff_list_words(int n) { return (n + 1) >> 1; }
-
-// The bitmap record replaces the numeric phase's pass over the row's products (about flop / 32
-// warp steps of loads and shared atomics) by a copy of the row's W bitmap words (about W / 32
+// The handoff replaces the numeric phase's pass over the row's products (about flop / 32 warp
+// steps of loads and shared atomics) by a copy of the row's W bitmap words (about W / 32
 // coalesced steps, written once by the symbolic phase); it pays unless the span is much wider
-// than the products. A list record (n / 2 words, n <= flop) always pays.
+// than the products.
 __host__ __device__ __forceinline__ bool handoff_pays(long long flop, long long words) {
   return 3 * flop >= words;
 }

@@ -163,10 +163,11 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     unsigned short* pre = reinterpret_cast<unsigned short*>(base + 4 * W);
     double* acc = reinterpret_cast<double*>(base + acc_off);              // n sums + spare
     unsigned short* coff = reinterpret_cast<unsigned short*>(base + acc_off + 8 * (n + 1));
-    // the symbolic phase's record of this row's columns, if it handed one off
-    const int hs = handoff.data ? handoff.slot[i] : -1;
-    const bool has_list = hs >= 0 && (hs & kHandoffList);
-    const unsigned* hrec = hs >= 0 ? handoff.data + (hs & (kHandoffList - 1)) : nullptr;
+    const unsigned* hbm = nullptr;   // the symbolic phase's bitmap of this row, if handed off
+    if (handoff.data) {
+      const int hs = handoff.slot[i];
+      if (hs >= 0) hbm = handoff.data + 32ll * hs;
+    }
     for (int t = lane; t < n; t += 32) acc[t] = 0.0;
     // the first chunk of A entries stays in registers
     int bs, len;
@@ -174,21 +175,9 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     load_chunk(A, B, rs, re, bs, len, &a);
     const int cnt = (re - rs) < 32 ? (re - rs) : 32;
     bool bad = false;
-    // 1) presence bitmap of the row's columns: from the handed-off column list (which also
-    //    gives C's columns in order), copied in, or built from the products
-    if (has_list) {
-      for (int w = lane; w < W; w += 32) bm[w] = 0u;
-      __syncwarp();
-      const unsigned short* lst = reinterpret_cast<const unsigned short*>(hrec);
-      for (int t = lane; t < n; t += 32) {
-        const unsigned off = __ldg(lst + t);
-        coff[t] = (unsigned short)off;
-        bad |= off >= (unsigned)span;
-        red_or_shared_if(off < (unsigned)span, bm + swz(off >> 5), 1u << (off & 31));
-      }
-      __syncwarp();
-    } else if (hrec) {
-      for (int w = lane; w < W; w += 32) bm[swz(w)] = __ldg(hrec + w);
+    // 1) presence bitmap of the row's columns: copied in, or built from the products
+    if (hbm) {
+      for (int w = lane; w < W; w += 32) bm[swz(w)] = __ldg(hbm + w);
       __syncwarp();
     } else {
       for (int w = lane; w < W; w += 32) bm[w] = 0u;
@@ -201,27 +190,15 @@ __global__ void __launch_bounds__(WPB * 32, BUDGET <= 4608 ? APPT_RANK_MIN_BLOCK
     const int running = bitmap_prefix32(bm, W, pre);
     __syncwarp();
     if (running != n) bad = true;
-    // 3) accumulate at the column's rank, k by k; remember the column of every rank (unless the
-    //    list gave them)
+    // 3) accumulate at the column's rank, k by k; remember the column of every rank
     if (running == n) {
-      if (has_list) {
-        accumulate_chunk_ranked<G, false>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre,
-                                          acc, coff);
-        for (int cb = rs + 32; cb < re; cb += 32) {
-          load_chunk(A, B, cb, re, bs, len, &a);
-          const int c2 = (re - cb) < 32 ? (re - cb) : 32;
-          accumulate_chunk_ranked<G, false>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre,
-                                            acc, coff);
-        }
-      } else {
-        accumulate_chunk_ranked<G>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre, acc,
+      accumulate_chunk_ranked<G>(B, bs, len, a, cnt, lo, (unsigned)span, n, bm, pre, acc,
+                                 coff);
+      for (int cb = rs + 32; cb < re; cb += 32) {
+        load_chunk(A, B, cb, re, bs, len, &a);
+        const int c2 = (re - cb) < 32 ? (re - cb) : 32;
+        accumulate_chunk_ranked<G>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre, acc,
                                    coff);
-        for (int cb = rs + 32; cb < re; cb += 32) {
-          load_chunk(A, B, cb, re, bs, len, &a);
-          const int c2 = (re - cb) < 32 ? (re - cb) : 32;
-          accumulate_chunk_ranked<G>(B, bs, len, a, c2, lo, (unsigned)span, n, bm, pre, acc,
-                                     coff);
-        }
       }
       // 4) the row is already in column order: one coalesced copy
       for (int t = lane; t < n; t += 32) {

@@ -186,48 +186,25 @@ __global__ void __launch_bounds__(WPB * 32, WORDS <= 1024 ? APPT_SYM_MIN_BLOCKS 
     __syncwarp();
     const bool bad = fill_row_bitmap_g<G>(A, B, rs, re, lo, (unsigned)span, bm);
     __syncwarp();
-    // count: each lane owns a run of W / 32 consecutive logical words (the run order is the
-    // column order, which the list record below needs)
-    const int per = W >> 5;
-    const unsigned w0 = (unsigned)lane * per;
-    int mine = 0;
-    for (int q = 0; q < per; ++q) mine += __popc(bm[swz(w0 + q)]);
-    const int incl = warp_incl_scan(mine);
-    const int cnt = __shfl_sync(kFull, incl, 31);
+    int cnt = 0;
+    for (int w = lane; w < W; w += 32) cnt += __popc(bm[w]);
+    cnt = warp_sum(cnt);
     if (__any_sync(kFull, bad) && lane == 0) set_error(err, kErrCapacity);
     if (lane == 0) row_nnz[i] = cnt;
-    if (handoff.data && handoff_fits_rank(W)) {
-      const int lw = handoff_list_words(cnt);
-      const bool as_list = lw < W;   // the sorted column list is the smaller record
-      const int need = as_list ? lw : W;
-      if (as_list || handoff_pays(flop, W)) {
-        if (chunk_cur + need > chunk_end) {
-          unsigned long long c = 0;
-          if (lane == 0) c = atomicAdd(handoff.top, (unsigned long long)kHandoffChunkWords);
-          c = __shfl_sync(kFull, c, 0);
-          chunk_cur = (long long)c;
-          chunk_end = chunk_cur + kHandoffChunkWords;
-          if (chunk_end > handoff.capacity) chunk_end = chunk_cur;   // arena exhausted
-        }
-        if (chunk_cur + need <= chunk_end) {
-          if (as_list) {   // column offsets j - lo in ascending order, lane runs in lane order
-            unsigned short* out = reinterpret_cast<unsigned short*>(handoff.data + chunk_cur);
-            int pos = incl - mine;
-            for (int q = 0; q < per; ++q) {
-              unsigned bits = bm[swz(w0 + q)];
-              while (bits) {
-                out[pos++] = (unsigned short)(32u * (w0 + q) + (unsigned)(__ffs(bits) - 1));
-                bits &= bits - 1u;
-              }
-            }
-            if (lane == 0) handoff.slot[i] = (int)chunk_cur | kHandoffList;
-          } else {
-            unsigned* out = handoff.data + chunk_cur;
-            for (int w = lane; w < W; w += 32) out[w] = bm[swz(w)];
-            if (lane == 0) handoff.slot[i] = (int)chunk_cur;
-          }
-          chunk_cur += need;
-        }
+    if (handoff.data && handoff_fits_rank(W) && handoff_pays(flop, W)) {
+      if (chunk_cur + W > chunk_end) {
+        unsigned long long c = 0;
+        if (lane == 0) c = atomicAdd(handoff.top, (unsigned long long)kHandoffChunkWords);
+        c = __shfl_sync(kFull, c, 0);
+        chunk_cur = (long long)c;
+        chunk_end = chunk_cur + kHandoffChunkWords;
+        if (chunk_end > handoff.capacity) chunk_end = chunk_cur;   // arena exhausted
+      }
+      if (chunk_cur + W <= chunk_end) {
+        unsigned* out = handoff.data + chunk_cur;
+        for (int w = lane; w < W; w += 32) out[w] = bm[swz(w)];
+        if (lane == 0) handoff.slot[i] = (int)(chunk_cur >> 5);
+        chunk_cur += W;
       }
     }
     __syncwarp();

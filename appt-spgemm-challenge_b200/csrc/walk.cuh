@@ -230,13 +230,12 @@ __device__ __forceinline__ int rank_or(const unsigned* bm, const unsigned short*
   return ok ? min(r, dummy) : dummy;
 }
 
-// Ranked accumulation over one chunk of A entries: acc[rank(j)] += a_ik * b_kj and, with COFF,
+// Ranked accumulation over one chunk of A entries: acc[rank(j)] += a_ik * b_kj and
 // coff[rank(j)] = j - lo for every product with j in the span, k-sequentially (G ordered
-// sub-phases per step when G > 1); without COFF the columns of the ranks are already known (a
-// handed-off column list). Lanes without a product in a (sub-)phase update the spare slot
-// acc[n] / coff[n] instead, so the step has no branch. In the common case the B entries of the
-// next two steps are loaded while the current step is applied.
-template <int G, bool COFF = true>
+// sub-phases per step when G > 1). Lanes without a product in a (sub-)phase update the
+// spare slot acc[n] / coff[n] instead, so the step has no branch. In the common case the B
+// entries of the next two steps are loaded while the current step is applied.
+template <int G>
 __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, int len, double a,
                                                         int cnt, int lo, unsigned span, int n,
                                                         const unsigned* bm,
@@ -272,7 +271,7 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
       for (int g = 0; g < G; ++g) {
         const int pos = (G == 1 || grp == g) ? r0 : n;
         acc[pos] = __dadd_rn(acc[pos], p0);
-        if (COFF) coff[pos] = (unsigned short)off0;
+        coff[pos] = (unsigned short)off0;
         __syncwarp();
       }
       off0 = off1;
@@ -299,7 +298,7 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
       for (int g = 0; g < G; ++g) {
         const int pos = (G == 1 || grp == g) ? r0 : n;
         acc[pos] = __dadd_rn(acc[pos], p0);
-        if (COFF) coff[pos] = (unsigned short)off0;
+        coff[pos] = (unsigned short)off0;
         __syncwarp();
       }
       off0 = (unsigned)(j1 - lo);
@@ -321,7 +320,7 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
             const unsigned off = (unsigned)(j - lo);
             const int pos = rank_or(bm, pre, off, span, n);
             acc[pos] = mul_add_rn(acc[pos], at, __ldg(B.val + bt + q));
-            if (COFF) coff[pos] = (unsigned short)off;
+            coff[pos] = (unsigned short)off;
           }
         }
         __syncwarp();
