@@ -361,6 +361,53 @@ def spgemm_device(rows: int, cols: int, nnz: int, row_ptr: int, col_idx: int, va
     return DeviceResult(out, st)
 
 
+class DeviceMultiply:
+    """Repeated C = op(A, B) on device-resident operands whose call arguments are built once:
+    each run() makes one appt_spgemm call (C stays on the device, in the library's pool) and
+    releases the previous run's C first. For loops that multiply the same resident operands
+    again and again, where rebuilding the ctypes arguments would cost host time per call."""
+
+    def __init__(self, rows: int, cols: int, nnz: int, row_ptr: int, col_idx: int, val: int,
+                 B: tuple | None = None, op: str = "ab", method: str = "adaptive",
+                 row_base: int = 0, stream: int | None = None, device: int = 0,
+                 timing: bool = False):
+        self._lib = load()
+        self._a = CsrIn(rows, cols, nnz, row_ptr, col_idx, val)
+        self._b = CsrIn(*B) if B is not None else None
+        self._bref = ct.byref(self._b) if self._b is not None else None
+        self._o = _options(op, method, MEM_DEVICE, MEM_DEVICE, row_base, stream, device, timing)
+        self._out = CsrOut()
+        self._st = Stats()
+        self._live = False
+        self.nnz = 0
+
+    def run(self) -> "DeviceMultiply":
+        self.free()
+        _check(self._lib.appt_spgemm(ct.byref(self._a), self._bref, ct.byref(self._o),
+                                     ct.byref(self._out), ct.byref(self._st)), "appt_spgemm")
+        self._live = True
+        self.nnz = int(self._out.nnz)
+        return self
+
+    def phase_ms(self, phase: str) -> float:
+        return float(self._st.ms_phase[PHASES.index(phase)])
+
+    @property
+    def stats(self) -> dict:
+        return self._st.as_dict()
+
+    def free(self) -> None:
+        if self._live:
+            self._lib.appt_free_out(ct.byref(self._out))
+            self._live = False
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
 def transpose(A: Csr, device: int = 0) -> Csr:
     lib = load()
     keep: list = []

@@ -129,6 +129,12 @@ class Communicator:
                "appt_comm_row_split")
         return [int(x) for x in out]
 
+    def multiply(self, A_block_spec, B_spec, op: str = "ab", row_base: int = 0,
+                 method: str = "adaptive", stream=None, timing: bool = False) -> "CommMultiply":
+        """A reusable call of this rank's block product on device-resident operands (see
+        CommMultiply)."""
+        return CommMultiply(self, A_block_spec, B_spec, op, row_base, method, stream, timing)
+
     def spgemm(self, A_block, B_spec, op: str = "ab", row_base: int = 0, out: str = "device",
                method: str = "adaptive", stream=None, timing: bool = False, copy: bool = True):
         """This rank's block of C. A_block: a host Csr, or a device spec tuple; B_spec: device
@@ -164,3 +170,52 @@ class Communicator:
             finally:
                 load().appt_free_out(ct.byref(res))
         return DeviceResult(res, st), offs
+
+
+class CommMultiply:
+    """This rank's block of C = op(A, B) on device-resident operands with its call arguments built
+    once: each run() makes one appt_comm_spgemm call (collective), releases the previous run's C
+    block first, and leaves the block's device C and the ranks' offsets in .nnz / .offsets."""
+
+    def __init__(self, comm: Communicator, A_block_spec, B_spec, op, row_base, method, stream,
+                 timing):
+        self._comm = comm
+        self._lib = load()
+        self._a = _spec_in(A_block_spec)
+        self._b = _spec_in(B_spec)
+        self._o = _options(op, method, MEM_DEVICE, MEM_DEVICE, row_base, stream, comm.device,
+                           timing, b_mem=B_DEVICE)
+        self._out = CsrOut()
+        self._st = Stats()
+        self.offsets = np.zeros(comm.nranks + 1, np.int64)
+        self._live = False
+        self.nnz = 0
+
+    def run(self) -> "CommMultiply":
+        self.free()
+        _check(self._lib.appt_comm_spgemm(self._comm._h, ct.byref(self._a), ct.byref(self._b),
+                                          ct.byref(self._o), ct.byref(self._out),
+                                          self.offsets.ctypes.data, ct.byref(self._st)),
+               "appt_comm_spgemm")
+        self._live = True
+        self.nnz = int(self._out.nnz)
+        return self
+
+    def phase_ms(self, phase: str) -> float:
+        from . import PHASES
+        return float(self._st.ms_phase[PHASES.index(phase)])
+
+    @property
+    def stats(self) -> dict:
+        return self._st.as_dict()
+
+    def free(self) -> None:
+        if self._live:
+            self._lib.appt_free_out(ct.byref(self._out))
+            self._live = False
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

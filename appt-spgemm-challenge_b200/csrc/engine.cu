@@ -77,6 +77,13 @@ struct DeviceCtx {
   cudaStream_t side[kSide] = {};
   cudaEvent_t ev_fork = nullptr;
   cudaEvent_t ev_join[kSide] = {};
+  // events reused by every call (calls on a device are serialised by `mu`): phase timing events
+  // (created on demand, kept), and the ordering events of host operands and host results
+  std::vector<cudaEvent_t> ev_timing;
+  static constexpr int kSinkEvents = 9;   // kSinkBlocks + 1
+  cudaEvent_t ev_sink[kSinkEvents] = {};
+  cudaEvent_t ev_staged[2] = {};           // operand allocations ordered before their copies
+  cudaEvent_t ev_values = nullptr;         // host operands' values in place
   std::mutex mu;
   bool ok = false;
 };
@@ -136,6 +143,10 @@ static int get_ctx(int device, DeviceCtx** out) {
       CK(cudaEventCreateWithFlags(&c.ev_join[j], cudaEventDisableTiming));
     }
     CK(cudaEventCreateWithFlags(&c.ev_fork, cudaEventDisableTiming));
+    for (int k = 0; k < DeviceCtx::kSinkEvents; ++k)
+      CK(cudaEventCreateWithFlags(&c.ev_sink[k], cudaEventDisableTiming));
+    for (int k = 0; k < 2; ++k) CK(cudaEventCreateWithFlags(&c.ev_staged[k], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&c.ev_values, cudaEventDisableTiming));
     cudaMemPoolProps props;
     std::memset(&props, 0, sizeof(props));
     props.allocType = cudaMemAllocationTypePinned;
@@ -216,6 +227,8 @@ struct Scratch {
 struct PhaseTimer {
   bool on = false;
   cudaStream_t s = nullptr;
+  std::vector<cudaEvent_t>* pool = nullptr;   // the device's reusable timing events
+  size_t used = 0;
   struct Mark {
     int phase;
     cudaEvent_t a, b;
@@ -224,25 +237,34 @@ struct PhaseTimer {
   cudaEvent_t t0 = nullptr, t1 = nullptr;
   int cur = -1;
   cudaEvent_t cur_a = nullptr;
-  void start(bool enable, cudaStream_t st) {
+  cudaEvent_t take() {
+    if (used == pool->size()) {
+      cudaEvent_t e = nullptr;
+      cudaEventCreate(&e);
+      pool->push_back(e);
+    }
+    return (*pool)[used++];
+  }
+  void start(bool enable, cudaStream_t st, std::vector<cudaEvent_t>* events) {
     on = enable;
     s = st;
+    pool = events;
+    used = 0;
     if (!on) return;
-    cudaEventCreate(&t0);
-    cudaEventCreate(&t1);
+    t0 = take();
+    t1 = take();
     cudaEventRecord(t0, s);
   }
   void begin(int phase) {
     if (!on) return;
     end();
     cur = phase;
-    cudaEventCreate(&cur_a);
+    cur_a = take();
     cudaEventRecord(cur_a, s);
   }
   void end() {
     if (!on || cur < 0) return;
-    cudaEvent_t b;
-    cudaEventCreate(&b);
+    cudaEvent_t b = take();
     cudaEventRecord(b, s);
     marks.push_back({cur, cur_a, b});
     cur = -1;
@@ -262,13 +284,8 @@ struct PhaseTimer {
         st->ms_phase[m.phase] += ms;
       }
     }
-    for (auto& m : marks) {
-      cudaEventDestroy(m.a);
-      cudaEventDestroy(m.b);
-    }
     marks.clear();
-    cudaEventDestroy(t0);
-    cudaEventDestroy(t1);
+    used = 0;   // the events go back to the device's pool
     on = false;
   }
   ~PhaseTimer() {
@@ -704,7 +721,7 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
       set_error("host allocation failed for C");
       return kErrOom;
     }
-    for (int k = 0; k <= K; ++k) CK(cudaEventCreateWithFlags(&evs[k], cudaEventDisableTiming));
+    for (int k = 0; k <= K; ++k) evs[k] = ctx->ev_sink[k];
     // row pointers first (converted to int32 for the reference layout)
     if (hd.rp32) {
       int* rp32 = sc.get<int>((size_t)m + 1);
@@ -764,7 +781,6 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
   tm.end();
   if (sink) {
     CK(cudaStreamSynchronize(cs));
-    for (int k = 0; k <= K; ++k) cudaEventDestroy(evs[k]);
     sink->done = true;
     sink->nnz = nnz;
   }
@@ -797,7 +813,7 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
 // (analyze, symbolic) overlap their copy -- the caller must make `s` wait for `vs` before any
 // kernel reads the values.
 static int stage_operand(const MatView& M, Scratch& sc, cudaStream_t s, Csr* out,
-                         cudaStream_t vs = nullptr) {
+                         cudaStream_t vs = nullptr, cudaEvent_t order_ev = nullptr) {
   int* rp = sc.get<int>((size_t)M.rows + 1);
   int* ci = sc.get<int>((size_t)M.nnz);
   double* val = sc.get<double>((size_t)M.nnz);
@@ -818,12 +834,9 @@ static int stage_operand(const MatView& M, Scratch& sc, cudaStream_t s, Csr* out
   }
   if (M.nnz > 0) {
     CK(cudaMemcpyAsync(ci, M.ci + rp0, sizeof(int) * (size_t)M.nnz, cudaMemcpyHostToDevice, s));
-    if (vs) {
-      cudaEvent_t alloc_done;
-      CK(cudaEventCreateWithFlags(&alloc_done, cudaEventDisableTiming));
-      CK(cudaEventRecord(alloc_done, s));
-      CK(cudaStreamWaitEvent(vs, alloc_done, 0));
-      cudaEventDestroy(alloc_done);
+    if (vs) {   // the values' stream waits for the allocation made on `s`
+      CK(cudaEventRecord(order_ev, s));
+      CK(cudaStreamWaitEvent(vs, order_ev, 0));
     }
     CK(cudaMemcpyAsync(val, M.val + rp0, sizeof(double) * (size_t)M.nnz, cudaMemcpyHostToDevice,
                        vs ? vs : s));
@@ -920,8 +933,7 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
       if (ev) {
         cudaStreamWaitEvent(s, ev, 0);
         cudaEventSynchronize(ev);   // host buffers stay untouched once this returns
-        cudaEventDestroy(ev);
-        ev = nullptr;
+        ev = nullptr;               // (the event belongs to the device context)
       }
     }
     ~ValuesReady() { wait(); }
@@ -929,7 +941,7 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
   const bool defer = opt.in_mem == 0 && ab && opt.method != kMethodEsc;
   cudaStream_t vs = defer ? ctx->copy_stream : nullptr;
   if (opt.in_mem == 0) {
-    rc = stage_operand(A, sc, s, &dA, vs);
+    rc = stage_operand(A, sc, s, &dA, vs, ctx->ev_staged[0]);
     if (rc) return rc;
   } else {
     dA = Csr{A.rp, A.ci, A.val, (int)A.rows, (int)A.cols};
@@ -943,7 +955,7 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
       }
       b_nnz = B->nnz;
       if (b_in == 0) {
-        rc = stage_operand(*B, sc, s, &dB, vs);
+        rc = stage_operand(*B, sc, s, &dB, vs, ctx->ev_staged[1]);
         if (rc) return rc;
       } else {
         dB = Csr{B->rp, B->ci, B->val, (int)B->rows, (int)B->cols};
@@ -968,7 +980,7 @@ static int run(const MatView& A, const MatView* B, const CallOptions& opt, Devic
   const int upper = (opt.op == kOpAATUpper || opt.op == kOpABUpper) ? 1 : 0;
   if (defer) {
     vals.s = s;
-    CK(cudaEventCreateWithFlags(&vals.ev, cudaEventDisableTiming));
+    vals.ev = ctx->ev_values;
     CK(cudaEventRecord(vals.ev, vs));
   }
   return multiply_device(ctx, dA, dB, A.nnz, b_nnz, upper, (int)opt.row_base, opt.method, s, sc,
@@ -1046,7 +1058,7 @@ static int spgemm_to_host(const MatView& A, const MatView* B, const CallOptions&
   CallStats* stp = st ? st : &local;
   *stp = CallStats();
   PhaseTimer tm;
-  tm.start(opt.timing != 0 || prof_env(), s);
+  tm.start(opt.timing != 0 || prof_env(), s, &ctx->ev_timing);
   DevC dc;
   {
     Scratch sc(ctx, s);
@@ -1175,7 +1187,7 @@ int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C
   CallStats* stp = st ? st : &local;
   *stp = CallStats();
   PhaseTimer tm;
-  tm.start(opt.timing != 0 || prof_env(), s);
+  tm.start(opt.timing != 0 || prof_env(), s, &ctx->ev_timing);
   DevC dc;
   {
     Scratch sc(ctx, s);

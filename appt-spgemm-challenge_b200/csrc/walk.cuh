@@ -226,7 +226,12 @@ __device__ __forceinline__ int rank_or(const unsigned* bm, const unsigned short*
                                        unsigned span, int dummy) {
   const bool ok = off < span;
   const unsigned w = ok ? swz(off >> 5) : 0u;
+#ifdef APPT_RANK_FUNNEL
+  // bits of the word below bit b: the word shifted left by 32 - b (nothing when b = 0)
+  const int r = (int)pre[w] + __popc(__funnelshift_l(0u, bm[w], 32u - (off & 31)));
+#else
   const int r = (int)pre[w] + __popc(bm[w] & ((1u << (off & 31)) - 1u));
+#endif
   return ok ? min(r, dummy) : dummy;
 }
 
@@ -235,6 +240,12 @@ __device__ __forceinline__ int rank_or(const unsigned* bm, const unsigned short*
 // sub-phases per step when G > 1). Lanes without a product in a (sub-)phase update the
 // spare slot acc[n] / coff[n] instead, so the step has no branch. In the common case the B
 // entries of the next two steps are loaded while the current step is applied.
+// Unroll factor of the rank tier's step loop (1: none).
+#ifndef APPT_RANK_UNROLL
+#define APPT_RANK_UNROLL 1
+#endif
+constexpr int kRankUnroll = APPT_RANK_UNROLL;
+
 template <int G>
 __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, int len, double a,
                                                         int cnt, int lo, unsigned span, int n,
@@ -257,6 +268,7 @@ __device__ __forceinline__ void accumulate_chunk_ranked(const Csr& B, int bs, in
                           sub, lo, &x1);
     unsigned off0 = (unsigned)(j0 - lo);
     int r0 = rank_or(bm, pre, off0, span, n);
+#pragma unroll kRankUnroll
     for (int t0 = 0; t0 < cnt; t0 += G) {
       // entries two steps ahead (a step past the chunk reads a valid row and is discarded)
       const int t2 = (t0 + 2 * G + grp) & 31;
