@@ -66,7 +66,8 @@ struct DeviceCtx {
   cudaMemPool_t pool = nullptr;        // per-call temporaries
   cudaMemPool_t pool_big = nullptr;    // allocations of 64 MiB and more (C, large scratch): kept
                                        // apart so small temporaries never split their blocks
-  char* stage = nullptr;   // pinned host staging for small device->host reads
+  char* stage = nullptr;       // pinned host staging for small device->host reads
+  char* stage_dev = nullptr;   // the same memory as the device addresses it (readback kernels)
   // bitmap handoff arena (symbolic -> numeric rank tier), allocated on first use and kept: calls
   // on a device are serialised by `mu` and each ends with its work complete
   unsigned* harena = nullptr;
@@ -158,6 +159,7 @@ static int get_ctx(int device, DeviceCtx** out) {
     CK(cudaMemPoolSetAttribute(c.pool, cudaMemPoolAttrReleaseThreshold, &thr));
     CK(cudaMemPoolSetAttribute(c.pool_big, cudaMemPoolAttrReleaseThreshold, &thr));
     CK(cudaMallocHost((void**)&c.stage, 4096));
+    CK(cudaHostGetDevicePointer((void**)&c.stage_dev, c.stage, 0));
     c.device = device;
     c.ok = true;
   }
@@ -459,16 +461,17 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   tm.begin(kPhScan);
   note_launches(scan_exclusive(row_nnz, crp, m, scs, s));
   char* stg = ctx->stage;
-  CK(cudaMemcpyAsync(stg, crp + m, 8, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(stg + 8, err, sizeof(int), cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(stg + 16, tflop, 8, cudaMemcpyDeviceToHost, s));
+  Readback rb;   // one kernel writes the values into the pinned stage
+  const int o_nnz = rb.add(crp + m, 8), o_flop = rb.add(tflop, 8), o_err = rb.add(err, 4);
+  launch_readback(rb, ctx->stage_dev, s);
+  note_launches(1);
   CK(cudaStreamSynchronize(s));
   long long nnz;
   int herr;
   unsigned long long hflop;
-  std::memcpy(&nnz, stg, 8);
-  std::memcpy(&herr, stg + 8, sizeof(int));
-  std::memcpy(&hflop, stg + 16, 8);
+  std::memcpy(&nnz, stg + o_nnz, 8);
+  std::memcpy(&herr, stg + o_err, sizeof(int));
+  std::memcpy(&hflop, stg + o_flop, 8);
   if (herr & kErrBounds) {
     set_error("operand index out of range (A column >= B rows)");
     return kErrInvalid;
@@ -670,23 +673,26 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
 
   // the one mid-pipeline synchronisation: C's size, the numeric bin sizes (and the blocks' first
   // entries in C)
+  // (one kernel writes them into the pinned stage)
   char* stg = ctx->stage;
-  for (int k = 1; k < K; ++k)
-    CK(cudaMemcpyAsync(stg + 1024 + 8 * k, crp + (long long)k * m / K, 8, cudaMemcpyDeviceToHost,
-                       s));
-  CK(cudaMemcpyAsync(stg, crp + m, 8, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(stg + 8, boff_num, 8 * (kNumNumBins + 1), cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(stg + 256, gst, sizeof(AnalyzeStats), cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(stg + 512, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  Readback rb;
+  const int o_nnz = rb.add(crp + m, 8);
+  const int o_boff = rb.add(boff_num, 8 * (kNumNumBins + 1));
+  const int o_gst = rb.add(gst, sizeof(AnalyzeStats));
+  const int o_err = rb.add(err, 4);
+  int o_cs[kSinkBlocks + 1] = {0};
+  for (int k = 1; k < K; ++k) o_cs[k] = rb.add(crp + (long long)k * m / K, 8);
+  launch_readback(rb, ctx->stage_dev, s);
+  note_launches(1);
   CK(cudaStreamSynchronize(s));
   long long nnz;
   long long boff[kNumNumBins + 1];
   AnalyzeStats hst;
   int herr;
-  std::memcpy(&nnz, stg, 8);
-  std::memcpy(boff, stg + 8, sizeof(boff));
-  std::memcpy(&hst, stg + 256, sizeof(hst));
-  std::memcpy(&herr, stg + 512, sizeof(int));
+  std::memcpy(&nnz, stg + o_nnz, 8);
+  std::memcpy(boff, stg + o_boff, sizeof(boff));
+  std::memcpy(&hst, stg + o_gst, sizeof(hst));
+  std::memcpy(&herr, stg + o_err, sizeof(int));
   if (herr & kErrBounds) {
     set_error("operand index out of range (A column >= B rows)");
     return kErrInvalid;
@@ -705,7 +711,7 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
   }
   long long cstart[kSinkBlocks + 1];
   cstart[0] = 0;
-  for (int k = 1; k < K; ++k) std::memcpy(&cstart[k], stg + 1024 + 8 * k, 8);
+  for (int k = 1; k < K; ++k) std::memcpy(&cstart[k], stg + o_cs[k], 8);
   cstart[K] = nnz;
   int* cci = sc.get<int>(nnz);
   double* cval = sc.get<double>(nnz);

@@ -139,6 +139,25 @@ void narrow_rowptr(const long long* in, int* out, long long n, cudaStream_t s);
 void block_bin_bounds(const int* rows, const long long* bin_off, int nb, long long m, int K,
                       long long* sub, cudaStream_t s);
 void iota(int* out, int n, cudaStream_t s);
+// Small device values read back at a synchronisation point: one kernel copies them (4-byte
+// words, sources 4-byte aligned) into a pinned host buffer, in list order, instead of one
+// device-to-host copy per value.
+struct Readback {
+  static constexpr int kMax = 16;
+  const void* src[kMax];
+  int words[kMax];
+  int n = 0;
+  // appends `bytes` (a multiple of 4) from src; returns the byte offset in the host buffer
+  int add(const void* p, int bytes) {
+    int off = 0;
+    for (int i = 0; i < n; ++i) off += 4 * words[i];
+    src[n] = p;
+    words[n] = bytes / 4;
+    ++n;
+    return off;
+  }
+};
+void launch_readback(const Readback& r, void* pinned_dst, cudaStream_t s);
 
 // analyze.cu
 // Lanes per row of the analysis of short rows (rows beyond 32 x that many entries take a CTA).

@@ -299,6 +299,21 @@ void iota(int* out, int n, cudaStream_t s) {
   iota_kernel<<<(n + 255) / 256, 256, 0, s>>>(out, n);
 }
 
+namespace {
+__global__ void readback_kernel(Readback r, unsigned* dst) {
+  int off = 0;
+  for (int i = 0; i < r.n; ++i) {
+    const unsigned* src = static_cast<const unsigned*>(r.src[i]);
+    for (int w = threadIdx.x; w < r.words[i]; w += blockDim.x) dst[off + w] = src[w];
+    off += r.words[i];
+  }
+}
+}  // namespace
+
+void launch_readback(const Readback& r, void* pinned_dst, cudaStream_t s) {
+  readback_kernel<<<1, 128, 0, s>>>(r, static_cast<unsigned*>(pinned_dst));
+}
+
 void smem_opt_in(const void* kern, size_t bytes) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {

@@ -58,8 +58,23 @@ STREAM_BLOCK_PRODUCTS = 1 << 32   # row blocks of streamed workloads: C <= 12 B 
 INT32_MAX = (1 << 31) - 1
 
 
-def _wl():
+# Reduced instances for ncu captures (--size profile): the same generators, a few GB on the
+# device at most, inputs or outputs still larger than L2.
+PROFILE_SIZES = {"stencil27": {"g": 48}, "uniform8": {}, "rmat": {"scale": 16},
+                 "banded": {"n": 1 << 20}, "zipf_att": {"rows": 1 << 14, "cols": 1 << 12}}
+
+
+def _wl(size: str = "full"):
     from appt_spgemm import matrices as M
+    if size == "profile":
+        gens = {"stencil27": M.stencil27, "uniform8": M.uniform8, "rmat": M.rmat,
+                "banded": M.banded, "zipf_att": M.zipf_att}
+        out = _wl("full")
+        for k, w in out.items():
+            kw = PROFILE_SIZES[k]
+            w["gen"] = (lambda g=gens[k], kw=kw: g(**kw))
+            w["name"] = w["name"] + "_profile" + "".join(f"_{a}{b}" for a, b in kw.items())
+        return out
     return {
         "stencil27": {"name": "stencil27_64cube_AxA", "op": "ab",
                       "gen": lambda: M.stencil27(64),
@@ -93,6 +108,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--block-products", type=int, default=STREAM_BLOCK_PRODUCTS,
                     help="products per row block of the streamed A*A^T workload")
+    ap.add_argument("--size", choices=["full", "profile"], default="full",
+                    help="profile: reduced instances for ncu captures (not a benchmark line)")
     return ap.parse_args()
 
 
@@ -264,7 +281,7 @@ def run_reference(args, rank: int, world: int):
     """The reference's own adaptive CUDA build on one GPU (rank 0 only)."""
     if rank != 0:
         return 0
-    wl = _wl()[args.workload]
+    wl = _wl(args.size)[args.workload]
     from appt_spgemm import matrices as M
     A = wl["gen"]()
     ref_bin = ROOT / "oracle" / "_ref" / "ref_spgemm"
@@ -454,7 +471,7 @@ def main():
     from appt_spgemm import distributed as D
     from appt_spgemm.streaming import cut_blocks, row_products_aat
 
-    wl = _wl()[args.workload]
+    wl = _wl(args.size)[args.workload]
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
