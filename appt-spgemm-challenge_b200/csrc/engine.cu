@@ -10,6 +10,7 @@
 //   * every failure returns a status instead of exiting the process.
 #include <cuda_runtime.h>
 #include <algorithm>
+#include <chrono>
 #include <functional>
 #include <atomic>
 #include <cmath>
@@ -299,6 +300,27 @@ enum Phase { kPhH2D = 0, kPhTranspose, kPhAnalyze, kPhSymbolic, kPhScan, kPhNume
 static const char* kPhaseNames[8] = {"h2d", "transpose", "analyze", "symbolic",
                                      "scan", "numeric",   "d2h",     "other"};
 
+// ------------------------------------------------------------------ host timeline
+// With APPT_PROF=2 the host-side moments of a call are recorded (microseconds since the call
+// began) and printed with the phase lines: where the host waits at the synchronisations and how
+// long it takes to issue the work around them.
+struct HostMarks {
+  bool on = false;
+  std::chrono::steady_clock::time_point t0;
+  std::vector<std::pair<const char*, double>> marks;
+  void start(bool enable) {
+    on = enable;
+    marks.clear();
+    if (on) t0 = std::chrono::steady_clock::now();
+  }
+  void mark(const char* what) {
+    if (!on) return;
+    marks.push_back({what, std::chrono::duration<double, std::micro>(
+                               std::chrono::steady_clock::now() - t0).count()});
+  }
+};
+static thread_local HostMarks t_marks;
+
 // ------------------------------------------------------------------ device pipeline
 // Called once per pipeline run with nnz(C), right after the mid-pipeline synchronisation that
 // learns it and before the numeric phase (multi-GPU calls post their nnz exchange from here).
@@ -465,7 +487,9 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   const int o_nnz = rb.add(crp + m, 8), o_flop = rb.add(tflop, 8), o_err = rb.add(err, 4);
   launch_readback(rb, ctx->stage_dev, s);
   note_launches(1);
+  t_marks.mark("issued up to the mid sync");
   CK(cudaStreamSynchronize(s));
+  t_marks.mark("mid sync returned");
   long long nnz;
   int herr;
   unsigned long long hflop;
@@ -498,7 +522,9 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   note_launches(1);
   tm.end();
   CK(cudaMemcpyAsync(stg + 8, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  t_marks.mark("numeric issued");
   CK(cudaStreamSynchronize(s));
+  t_marks.mark("final sync returned");
   std::memcpy(&herr, stg + 8, sizeof(int));
   if (herr) {
     set_error("numeric phase reported device error bits " + std::to_string(herr));
@@ -684,7 +710,9 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
   for (int k = 1; k < K; ++k) o_cs[k] = rb.add(crp + (long long)k * m / K, 8);
   launch_readback(rb, ctx->stage_dev, s);
   note_launches(1);
+  t_marks.mark("issued up to the mid sync");
   CK(cudaStreamSynchronize(s));
+  t_marks.mark("mid sync returned");
   long long nnz;
   long long boff[kNumNumBins + 1];
   AnalyzeStats hst;
@@ -791,7 +819,9 @@ static int multiply_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, long l
     sink->nnz = nnz;
   }
   CK(cudaMemcpyAsync(stg + 512, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  t_marks.mark("numeric issued");
   CK(cudaStreamSynchronize(s));
+  t_marks.mark("final sync returned");
   std::memcpy(&herr, stg + 512, sizeof(int));
   if (herr) {
     set_error("numeric phase reported device error bits " + std::to_string(herr));
@@ -900,6 +930,10 @@ static int do_transpose(DeviceCtx* ctx, Csr A, long long nnz, Scratch& sc, cudaS
 }
 
 static bool prof_env() { return env_flag("APPT_PROF"); }
+static int prof_level() {
+  const char* e = std::getenv("APPT_PROF");
+  return e && *e ? std::atoi(e) : 0;
+}
 
 // Per-phase device times in the reference's HashProf line format (include/hash_prof.h:9-28:
 // "[<tag>] <phase, left-aligned in 16> <ms, %7.3f> ms", then "[<tag>] TOTAL(GPU) ..."), on
@@ -908,6 +942,7 @@ static void print_prof(const char* tag, const CallStats& st) {
   for (int p = 0; p < 8; ++p)
     if (st.ms_phase[p] > 0.0) fprintf(stderr, "[%s] %-16s %7.3f ms\n", tag, kPhaseNames[p], st.ms_phase[p]);
   fprintf(stderr, "[%s] TOTAL(GPU)      %7.3f ms\n", tag, st.ms_total);
+  for (auto& m : t_marks.marks) fprintf(stderr, "[%s-host] %9.1f us  %s\n", tag, m.second, m.first);
 }
 
 // Core call. Returns C in device memory (pool allocations) in *dc.
@@ -1065,6 +1100,7 @@ static int spgemm_to_host(const MatView& A, const MatView* B, const CallOptions&
   *stp = CallStats();
   PhaseTimer tm;
   tm.start(opt.timing != 0 || prof_env(), s, &ctx->ev_timing);
+  t_marks.start(prof_level() >= 2);
   DevC dc;
   {
     Scratch sc(ctx, s);
@@ -1121,6 +1157,7 @@ static int spgemm_to_host(const MatView& A, const MatView* B, const CallOptions&
       rc = kErrCuda;
     }
   }
+  t_marks.mark("call returns");
   if (prof_env() && rc == kOk) print_prof(opt.prof_tag, *stp);
   return rc;
 }
@@ -1194,6 +1231,7 @@ int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C
   *stp = CallStats();
   PhaseTimer tm;
   tm.start(opt.timing != 0 || prof_env(), s, &ctx->ev_timing);
+  t_marks.start(prof_level() >= 2);
   DevC dc;
   {
     Scratch sc(ctx, s);
@@ -1225,6 +1263,7 @@ int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C
       return kErrCuda;
     }
   }
+  t_marks.mark("call returns");
   if (prof_env() && rc == kOk) print_prof(opt.prof_tag, *stp);
   return rc;
 }
