@@ -484,7 +484,7 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   note_launches(scan_exclusive(row_nnz, crp, m, scs, s));
   char* stg = ctx->stage;
   Readback rb;   // one kernel writes the values into the pinned stage
-  const int o_nnz = rb.add(crp + m, 8), o_flop = rb.add(tflop, 8), o_err = rb.add(err, 4);
+  const int o_nnz = rb.add(crp + m, 8), o_flop = rb.add(tflop, 8), o_err = rb.add(err, 8);
   launch_readback(rb, ctx->stage_dev, s);
   note_launches(1);
   t_marks.mark("issued up to the mid sync");
@@ -493,8 +493,10 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   long long nnz;
   int herr;
   unsigned long long hflop;
+  int max_need = 0;   // err[1]: the largest per-row rank-tier budget
   std::memcpy(&nnz, stg + o_nnz, 8);
   std::memcpy(&herr, stg + o_err, sizeof(int));
+  std::memcpy(&max_need, stg + o_err + 4, sizeof(int));
   std::memcpy(&hflop, stg + o_flop, 8);
   if (herr & kErrBounds) {
     set_error("operand index out of range (A column >= B rows)");
@@ -518,7 +520,7 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   }
   tm.begin(kPhNumeric);
   if (vals_ready) CK(cudaStreamWaitEvent(s, vals_ready, 0));
-  launch_numeric_rank_all(boff, m, gidx, A, B, lo, hi, crp, cci, cval, err, sms, s);
+  launch_numeric_rank_all(boff, m, gidx, max_need, A, B, lo, hi, crp, cci, cval, err, sms, s);
   note_launches(1);
   tm.end();
   CK(cudaMemcpyAsync(stg + 8, err, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -543,7 +545,8 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
     st->products = (long long)hflop;
     st->c_nnz = nnz;
     st->method_used = kMethodAdaptive;
-    st->bin_rows[kNumRank8K + gidx] = m;
+    const int tier = max_need <= 2304 ? kNumRank2K : max_need <= 4608 ? kNumRank4K : kNumRank8K;
+    st->bin_rows[tier + gidx] = m;
   }
   return kOk;
 }

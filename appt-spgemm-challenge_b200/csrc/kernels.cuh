@@ -193,9 +193,11 @@ int build_dense_rows(Csr B, int* id, int* list, unsigned* bits, unsigned* pre, l
 void launch_symbolic_small(Csr A, Csr B, int upper, int row_base, int gidx, int* lo, int* hi,
                            int* row_nnz, long long* bin_off, unsigned long long* total_flop,
                            int* err, int num_sms, cudaStream_t s);
-void launch_numeric_rank_all(const long long* bin_off, long long m, int gidx, Csr A, Csr B,
-                             const int* lo, const int* hi, const long long* crp, int* cci,
-                             double* cval, int* err, int num_sms, cudaStream_t s);
+// max_need: the largest per-row rank-tier budget in bytes (the symbolic pass leaves it in err[1]);
+// the launch uses the smallest budget (2304, 4608 or 9216 bytes per warp) that covers it.
+void launch_numeric_rank_all(const long long* bin_off, long long m, int gidx, int max_need,
+                             Csr A, Csr B, const int* lo, const int* hi, const long long* crp,
+                             int* cci, double* cval, int* err, int num_sms, cudaStream_t s);
 
 // numeric.cu
 // row_counter: a zeroed int (the CTA tiers take rows from it dynamically)

@@ -714,11 +714,19 @@ void run_warp_rank(int bin, int gidx, const int* rows, const long long* bin_off,
 
 }  // namespace
 
-void launch_numeric_rank_all(const long long* bin_off, long long m, int gidx, Csr A, Csr B,
-                             const int* lo, const int* hi, const long long* crp, int* cci,
-                             double* cval, int* err, int num_sms, cudaStream_t s) {
-  run_warp_rank<9216, 4>(0, gidx, nullptr, bin_off, m, A, B, 0, 0, lo, hi, nullptr,
-                         RowBitmaps{}, crp, cci, cval, err, num_sms, s);
+void launch_numeric_rank_all(const long long* bin_off, long long m, int gidx, int max_need,
+                             Csr A, Csr B, const int* lo, const int* hi, const long long* crp,
+                             int* cci, double* cval, int* err, int num_sms, cudaStream_t s) {
+  // the smallest per-warp budget every row fits (more warps per SM for small rows)
+  if (max_need <= 2304)
+    run_warp_rank<2304, 8>(0, gidx, nullptr, bin_off, m, A, B, 0, 0, lo, hi, nullptr,
+                           RowBitmaps{}, crp, cci, cval, err, num_sms, s);
+  else if (max_need <= 4608)
+    run_warp_rank<4608, 8>(0, gidx, nullptr, bin_off, m, A, B, 0, 0, lo, hi, nullptr,
+                           RowBitmaps{}, crp, cci, cval, err, num_sms, s);
+  else
+    run_warp_rank<9216, 4>(0, gidx, nullptr, bin_off, m, A, B, 0, 0, lo, hi, nullptr,
+                           RowBitmaps{}, crp, cci, cval, err, num_sms, s);
 }
 
 void launch_numeric(int bin, const int* rows, const long long* bin_off, long long nrows, Csr A,

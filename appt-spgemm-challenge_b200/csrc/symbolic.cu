@@ -412,7 +412,9 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
     if (lane == 0) {
       row_nnz[i] = cnt;
       if (fbad) set_error(err, kErrCapacity);
-      if (6ll * W + 10ll * (cnt + 1) > kRankMaxBudget) set_error(err, kErrSmallFallback);
+      const long long need = 6ll * W + 10ll * (cnt + 1);   // the row's rank-tier budget
+      if (need > kRankMaxBudget) set_error(err, kErrSmallFallback);
+      else atomicMax(err + 1, (int)need);   // the numeric launch picks the smallest budget
     }
     __syncwarp();
   }
