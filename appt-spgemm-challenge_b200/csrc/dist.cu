@@ -22,6 +22,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -118,6 +119,13 @@ struct Comm {
   std::mutex mu;
 };
 
+// Host polling of a pending exchange spins (yielding the core) for this long before it falls back
+// to 20 us sleeps: a Linux sleep of 20 us returns after 60 us or more, and a rank that wakes late
+// starts its next product late, which the other ranks then wait for at their next exchange.
+#ifndef APPT_COMM_SPIN_US
+#define APPT_COMM_SPIN_US 2000
+#endif
+
 // Waits for `done` on the host, polling, for at most timeout_s(); aborts the communicator on
 // expiry or on an asynchronous NCCL error (that ends its pending kernels).
 static int wait_bounded(Comm* c, const char* what) {
@@ -143,7 +151,10 @@ static int wait_bounded(Comm* c, const char* what) {
                 "; the communicator was aborted");
       return kErrCuda;
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
+    if (el * 1e6 < APPT_COMM_SPIN_US)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
 }
 
@@ -397,25 +408,42 @@ int comm_spgemm(Comm* c, const MatView& A, const MatView* B, CallOptions opt, Ma
   }
   std::lock_guard<std::mutex> lk(c->mu);
   opt.device = c->device;
+  using clk = std::chrono::steady_clock;
+  const clk::time_point t0 = clk::now();
+  clk::time_point t_post = t0;
   bool posted = false;
   int post_rc = kOk;
   const std::function<int(long long)> hook = [&](long long nnz) {
     posted = true;
     post_rc = post_nnz(c, nnz);
+    t_post = clk::now();
     return post_rc;
   };
   opt.on_nnz = &hook;
   rc = spgemm(A, B, opt, C, st);
+  const clk::time_point t_pipe = clk::now();
   // every rank takes part in the exchange, failed or not, so that no rank waits for ever
   if (!posted) post_rc = post_nnz(c, -1);
   if (post_rc) {
     if (rc == kOk) free_out(C);
     return post_rc;
   }
+  const bool ready = cudaEventQuery(c->done) == cudaSuccess;
   const int wrc = wait_bounded(c, "nnz exchange");
   if (wrc) {
     if (rc == kOk) free_out(C);
     return wrc;
+  }
+  const char* pe = std::getenv("APPT_PROF");
+  if (pe && std::atoi(pe) >= 2) {
+    auto us = [&](clk::time_point t) {
+      return std::chrono::duration<double, std::micro>(t - t0).count();
+    };
+    fprintf(stderr,
+            "[%s-host] rank %d/%d: exchange posted %.1f us, call returned %.1f us, exchange "
+            "%s, done %.1f us\n",
+            opt.prof_tag, c->rank, c->nranks, us(t_post), us(t_pipe),
+            ready ? "already complete" : "waited for", us(clk::now()));
   }
   offsets[0] = 0;
   bool peer_failed = false;

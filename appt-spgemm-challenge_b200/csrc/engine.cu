@@ -449,8 +449,11 @@ static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, 
 // Small problems: one unbinned symbolic pass and one rank-tier launch over all rows, a handful of
 // launches instead of the binned pipeline's dozens. *fallback is set (nothing computed) when a
 // row does not fit; the caller then runs the general pipeline.
-constexpr long long kSmallRows = 65536;
-constexpr long long kSmallNnz = 1 << 21;
+#ifndef APPT_SMALL_ROWS
+#define APPT_SMALL_ROWS 65536
+#endif
+constexpr long long kSmallRows = APPT_SMALL_ROWS;
+constexpr long long kSmallNnz = 32 * kSmallRows;
 
 static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, int row_base,
                         cudaStream_t s, Scratch& sc, PhaseTimer& tm, DevC* C, CallStats* st,
