@@ -448,9 +448,11 @@ static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, 
 
 // Small problems: one unbinned symbolic pass and one rank-tier launch over all rows, a handful of
 // launches instead of the binned pipeline's dozens. *fallback is set (nothing computed) when a
-// row does not fit; the caller then runs the general pipeline.
+// row does not fit; the caller then runs the general pipeline. The row limit is measured: a
+// 2^17-row block of the 64^3 stencil or of a banded matrix runs 10-13 % faster here than binned,
+// a whole 2^18-row stencil 4 % slower.
 #ifndef APPT_SMALL_ROWS
-#define APPT_SMALL_ROWS 65536
+#define APPT_SMALL_ROWS 131072
 #endif
 constexpr long long kSmallRows = APPT_SMALL_ROWS;
 constexpr long long kSmallNnz = 32 * kSmallRows;

@@ -335,7 +335,9 @@ void launch_sym_warp(int bin, const int* rows, const long long* bin_off, Csr A, 
 // Small problems: warp per row over every row of A (no binning) computes the row's column span
 // and exact count in one pass with a bitmap of at most WORDS words, writes lo / hi for the rank
 // tier, and sets kErrSmallFallback (row_nnz 0) for a row whose bitmap or rank-tier layout would
-// not fit, after which the caller runs the general pipeline. bin_off receives {0, m}.
+// not fit, after which the caller runs the general pipeline. Once that flag is set every warp stops
+// at its next row (the pass's results are discarded, and the general pipeline's analyze repeats
+// the bounds check). bin_off receives {0, m}.
 template <int WORDS, int WPB, int G>
 __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int upper,
                                                             int row_base, int* lo_arr,
@@ -352,6 +354,7 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
     bin_off[1] = m;
   }
   for (long long r = (long long)blockIdx.x * WPB + warp; r < m; r += (long long)gridDim.x * WPB) {
+    if (__shfl_sync(kFull, *(volatile const int*)err, 0) & kErrSmallFallback) break;
     const int i = (int)r;
     const int rs = A.rp[i], re = A.rp[i + 1];
     int lo = INT_MAX, hi = -1, bad = 0;

@@ -257,22 +257,21 @@ class ClockSampler:
 
 
 def traffic_from_profiles(tag: str, workload: str, rows: int):
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary
-    profiles/<tag>.txt, used only when that summary was captured on this very workload and row
-    count (its "workload:" line reads "<name> rows=<rows>"); else (None, None)."""
-    f = ROOT / "profiles" / f"{tag}.txt"
-    if not f.exists():
-        return None, None
-    want = f"{workload} rows={rows}"
-    lines = f.read_text().splitlines()
-    if not any(ln.strip() == f"workload: {want}" for ln in lines):
-        return None, None
-    for ln in lines:
-        if ln.startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(ln.split(":", 1)[1].strip()), str(f.relative_to(ROOT))
-            except ValueError:
-                return None, None
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary
+    profiles/<tag>*.txt, used only when that summary names this very workload and row count (its
+    "workload:" line reads "<name> rows=<rows>"; a summary captured on a smaller case of a uniform
+    workload carries the traffic scaled to the full launch, and says so); else (None, None)."""
+    want = f"workload: {workload} rows={rows}"
+    for f in sorted((ROOT / "profiles").glob(f"{tag}*.txt")):
+        lines = f.read_text().splitlines()
+        if not any(ln.strip() == want for ln in lines):
+            continue
+        for ln in lines:
+            if ln.startswith("traffic_bytes_per_launch:"):
+                try:
+                    return float(ln.split(":", 1)[1].strip()), str(f.relative_to(ROOT))
+                except ValueError:
+                    return None, None
     return None, None
 
 
