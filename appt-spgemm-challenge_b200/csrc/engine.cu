@@ -430,6 +430,7 @@ static int esc_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper, 
   launch_esc_compress(m, foff, keys, vals, crp, cci, cval, sms, s);
   note_launches(m > 0 ? 1 : 0);
   tm.end();
+  CK(cudaStreamSynchronize(s));   // the call returns with C complete, like the other methods
   sc.detach(crp);
   sc.detach(cci);
   sc.detach(cval);
@@ -466,8 +467,8 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   int *lo, *hi, *row_nnz, *err;
   long long *boff, *scs;
   unsigned long long* tflop;
-  sc.carve([&](Carver& c) {   // err and tflop first: one memset clears both
-    err = c.take<int>(4);
+  sc.carve([&](Carver& c) {   // err (with the stop word 128 bytes on) and tflop first: one
+    err = c.take<int>(64);     // memset clears them
     tflop = c.take<unsigned long long>(1);
     lo = c.take<int>(m);
     hi = c.take<int>(m);
@@ -483,7 +484,8 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   CK(cudaMemsetAsync(err, 0, (char*)(tflop + 1) - (char*)err, s));
   const int gidx = group_index(a_nnz, m);   // B rows' average length taken from A's
   tm.begin(kPhSymbolic);
-  launch_symbolic_small(A, B, upper, row_base, gidx, lo, hi, row_nnz, boff, tflop, err, sms, s);
+  launch_symbolic_small(A, B, upper, row_base, gidx, lo, hi, row_nnz, boff, tflop, err, err + 32,
+                        sms, s);
   note_launches(1);
   tm.begin(kPhScan);
   note_launches(scan_exclusive(row_nnz, crp, m, scs, s));
@@ -1154,8 +1156,8 @@ static int spgemm_to_host(const MatView& A, const MatView* B, const CallOptions&
       set_error(std::string("D2H of C: ") + cudaGetErrorString(e));
       rc = kErrCuda;
     }
+    tm.finish(stp);   // before the scratch frees are queued (the stream is idle here)
   }
-  tm.finish(stp);
   stp->launches = kernel_launches() - launches0;
   sink->cols = dc.cols;
   if (rc == kOk) {
@@ -1256,8 +1258,10 @@ int spgemm(const MatView& A, const MatView* B, const CallOptions& opt, MatOut* C
       cudaFreeAsync(dc.ci, s);
       cudaFreeAsync(dc.val, s);
     }
+    // before the scratch frees are queued: the pipeline ended with a synchronisation, so the
+    // closing event completes at once instead of one more round trip behind the frees
+    tm.finish(stp);
   }
-  tm.finish(stp);
   stp->launches = kernel_launches() - launches0;
   if (rc == kOk) {
     C->rows = dc.rows;

@@ -335,16 +335,18 @@ void launch_sym_warp(int bin, const int* rows, const long long* bin_off, Csr A, 
 // Small problems: warp per row over every row of A (no binning) computes the row's column span
 // and exact count in one pass with a bitmap of at most WORDS words, writes lo / hi for the rank
 // tier, and sets kErrSmallFallback (row_nnz 0) for a row whose bitmap or rank-tier layout would
-// not fit, after which the caller runs the general pipeline. Once that flag is set every warp stops
-// at its next row (the pass's results are discarded, and the general pipeline's analyze repeats
-// the bounds check). bin_off receives {0, m}.
+// not fit, after which the caller runs the general pipeline. Such a row also sets *stop (a word
+// on a cache line of its own, away from the per-row atomics on err), and every warp stops one row
+// after it sees it: the word is read at the start of a row and tested at the start of the next,
+// so the read's latency hides behind the row's work (the pass's results are then discarded, and
+// the general pipeline's analyze repeats the bounds check). bin_off receives {0, m}.
 template <int WORDS, int WPB, int G>
 __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int upper,
                                                             int row_base, int* lo_arr,
                                                             int* hi_arr, int* row_nnz,
                                                             long long* bin_off,
                                                             unsigned long long* total_flop,
-                                                            int* err) {
+                                                            int* err, int* stop) {
   extern __shared__ unsigned sym_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned* bm = sym_smem + warp * WORDS;
@@ -353,8 +355,10 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
     bin_off[0] = 0;
     bin_off[1] = m;
   }
+  int stop_seen = 0;   // *stop as read at the start of the previous row
   for (long long r = (long long)blockIdx.x * WPB + warp; r < m; r += (long long)gridDim.x * WPB) {
-    if (__shfl_sync(kFull, *(volatile const int*)err, 0) & kErrSmallFallback) break;
+    if (__shfl_sync(kFull, stop_seen, 0)) break;
+    stop_seen = *(volatile const int*)stop;
     const int i = (int)r;
     const int rs = A.rp[i], re = A.rp[i + 1];
     int lo = INT_MAX, hi = -1, bad = 0;
@@ -401,6 +405,7 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
     if (W > WORDS || 6ll * W + 20 > kRankMaxBudget) {
       if (lane == 0) {
         set_error(err, kErrSmallFallback);
+        *(volatile int*)stop = 1;
         row_nnz[i] = 0;
       }
       continue;
@@ -416,8 +421,12 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
       row_nnz[i] = cnt;
       if (fbad) set_error(err, kErrCapacity);
       const long long need = 6ll * W + 10ll * (cnt + 1);   // the row's rank-tier budget
-      if (need > kRankMaxBudget) set_error(err, kErrSmallFallback);
-      else atomicMax(err + 1, (int)need);   // the numeric launch picks the smallest budget
+      if (need > kRankMaxBudget) {
+        set_error(err, kErrSmallFallback);
+        *(volatile int*)stop = 1;
+      } else {
+        atomicMax(err + 1, (int)need);   // the numeric launch picks the smallest budget
+      }
     }
     __syncwarp();
   }
@@ -425,8 +434,8 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
 
 template <int G>
 void run_sym_small(Csr A, Csr B, int upper, int row_base, int* lo, int* hi, int* row_nnz,
-                   long long* bin_off, unsigned long long* total_flop, int* err, int num_sms,
-                   cudaStream_t s) {
+                   long long* bin_off, unsigned long long* total_flop, int* err, int* stop,
+                   int num_sms, cudaStream_t s) {
   constexpr int WORDS = 1536, WPB = 8;
   const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
   auto kern = sym_small_kernel<WORDS, WPB, G>;
@@ -435,7 +444,7 @@ void run_sym_small(Csr A, Csr B, int upper, int row_base, int* lo, int* hi, int*
   if (blocks > (long long)num_sms * 4) blocks = (long long)num_sms * 4;
   if (blocks < 1) blocks = 1;
   kern<<<(unsigned)blocks, WPB * 32, smem, s>>>(A, B, upper, row_base, lo, hi, row_nnz, bin_off,
-                                                total_flop, err);
+                                                total_flop, err, stop);
 }
 
 }  // namespace
@@ -501,16 +510,16 @@ int build_dense_rows(Csr B, int* id, int* list, unsigned* bits, unsigned* pre, l
 
 void launch_symbolic_small(Csr A, Csr B, int upper, int row_base, int gidx, int* lo, int* hi,
                            int* row_nnz, long long* bin_off, unsigned long long* total_flop,
-                           int* err, int num_sms, cudaStream_t s) {
+                           int* err, int* stop, int num_sms, cudaStream_t s) {
   if (gidx == 2)
-    run_sym_small<4>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, num_sms,
-                     s);
+    run_sym_small<4>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, stop,
+                     num_sms, s);
   else if (gidx == 1)
-    run_sym_small<2>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, num_sms,
-                     s);
+    run_sym_small<2>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, stop,
+                     num_sms, s);
   else
-    run_sym_small<1>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, num_sms,
-                     s);
+    run_sym_small<1>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, stop,
+                     num_sms, s);
 }
 
 void launch_symbolic(int bin, const int* rows, const long long* bin_off, Csr A, Csr B, int upper,

@@ -110,7 +110,33 @@ def parse_args():
                     help="products per row block of the streamed A*A^T workload")
     ap.add_argument("--size", choices=["full", "profile"], default="full",
                     help="profile: reduced instances for ncu captures (not a benchmark line)")
+    ap.add_argument("--clock-poll-ms", type=float, default=2.0,
+                    help="NVML clock sampling interval during the timed region")
+    ap.add_argument("--bind-cpus", choices=["off", "gpu"], default="off",
+                    help="gpu: run each rank on the CPUs NVML reports as local to its GPU")
     return ap.parse_args()
+
+
+def bind_to_gpu_cpus(device: int):
+    """Restrict this process to the CPU cores NVML reports as nearest to `device` (its NUMA
+    node); returns the number of cores, or None when NVML cannot tell."""
+    try:
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(device)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        n = (os.cpu_count() + 63) // 64
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, n)
+        cpus = {64 * w + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return len(cpus)
+    except Exception:
+        return None
 
 
 def config_of(wl, A, c_nnz, products, method, world) -> dict:
@@ -148,13 +174,14 @@ def compulsory_bytes(A, B_rp, r0: int, r1: int, c_nnz: int) -> int:
 
 
 class NvmlClockSampler:
-    """SM clocks and throttle reasons during the timed region, polled through NVML every 2 ms
-    (the timed regions are milliseconds long, too short for nvidia-smi's loop)."""
+    """SM clocks and throttle reasons during the timed region, polled through NVML (every 2 ms by
+    default, --clock-poll-ms; the timed regions are milliseconds long, too short for
+    nvidia-smi's loop)."""
 
     REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device: int):
+    def __init__(self, device: int, poll_ms: float = 2.0):
         import pynvml
         import torch
         self.nv = pynvml
@@ -167,6 +194,7 @@ class NvmlClockSampler:
         self.mask = 0
         self.stop_flag = threading.Event()
         self.thread = None
+        self.poll_s = max(poll_ms, 0.1) * 1e-3
 
     def _run(self):
         nv = self.nv
@@ -176,7 +204,7 @@ class NvmlClockSampler:
                 self.mask |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
             except Exception:
                 pass
-            time.sleep(0.002)
+            time.sleep(self.poll_s)
 
     def start(self):
         self.thread = threading.Thread(target=self._run, daemon=True)
@@ -191,9 +219,9 @@ class NvmlClockSampler:
                 "source": "nvml"}
 
 
-def clock_sampler(device: int):
+def clock_sampler(device: int, poll_ms: float = 2.0):
     try:
-        return NvmlClockSampler(device)
+        return NvmlClockSampler(device, poll_ms)
     except Exception:
         return ClockSampler(device)
 
@@ -471,6 +499,7 @@ def main():
     from appt_spgemm.streaming import cut_blocks, row_products_aat
 
     wl = _wl(args.size)[args.workload]
+    bound = bind_to_gpu_cpus(local) if args.bind_cpus == "gpu" else None
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
@@ -567,7 +596,7 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
 
-    clk = clock_sampler(local)
+    clk = clock_sampler(local, args.clock_poll_ms)
     clk.start()
     launches0 = ap.kernel_launches()
     step_ms, num_ms = [], []
@@ -639,6 +668,8 @@ def main():
             "config": config_of(wl, A, all_cnnz, all_products, args.method, world),
             "l2": "flushed between steps (256 MB write)",
             "row_blocks_per_rank": len(blocks) - 1, "b_replication_ms": t_rep,
+            "host": {"cpu_binding": f"GPU-local cores ({bound})" if bound else "none",
+                     "clock_poll_ms": args.clock_poll_ms},
             "effective_gbs": cbytes / (t_total_max / args.steps * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": tr,
