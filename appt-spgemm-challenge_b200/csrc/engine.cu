@@ -467,8 +467,8 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   int *lo, *hi, *row_nnz, *err;
   long long *boff, *scs;
   unsigned long long* tflop;
-  sc.carve([&](Carver& c) {   // err (with the stop word 128 bytes on) and tflop first: one
-    err = c.take<int>(64);     // memset clears them
+  sc.carve([&](Carver& c) {   // err and tflop first: one memset clears both
+    err = c.take<int>(4);
     tflop = c.take<unsigned long long>(1);
     lo = c.take<int>(m);
     hi = c.take<int>(m);
@@ -484,8 +484,7 @@ static int small_device(DeviceCtx* ctx, Csr A, Csr B, long long a_nnz, int upper
   CK(cudaMemsetAsync(err, 0, (char*)(tflop + 1) - (char*)err, s));
   const int gidx = group_index(a_nnz, m);   // B rows' average length taken from A's
   tm.begin(kPhSymbolic);
-  launch_symbolic_small(A, B, upper, row_base, gidx, lo, hi, row_nnz, boff, tflop, err, err + 32,
-                        sms, s);
+  launch_symbolic_small(A, B, upper, row_base, gidx, lo, hi, row_nnz, boff, tflop, err, sms, s);
   note_launches(1);
   tm.begin(kPhScan);
   note_launches(scan_exclusive(row_nnz, crp, m, scs, s));

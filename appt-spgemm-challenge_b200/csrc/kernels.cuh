@@ -189,11 +189,10 @@ int build_dense_rows(Csr B, int* id, int* list, unsigned* bits, unsigned* pre, l
 
 // Small problems (symbolic.cu / numeric.cu): one unbinned symbolic pass over all rows, then the
 // 9 KB rank tier over all rows; kErrSmallFallback means some row does not fit (run the general
-// pipeline instead). bin_off: 2 int64, set to {0, m} by the symbolic pass. stop: a zeroed int on
-// a cache line other than err's, set with the fallback so that the other warps stop early.
+// pipeline instead). bin_off: 2 int64, set to {0, m} by the symbolic pass.
 void launch_symbolic_small(Csr A, Csr B, int upper, int row_base, int gidx, int* lo, int* hi,
                            int* row_nnz, long long* bin_off, unsigned long long* total_flop,
-                           int* err, int* stop, int num_sms, cudaStream_t s);
+                           int* err, int num_sms, cudaStream_t s);
 // max_need: the largest per-row rank-tier budget in bytes (the symbolic pass leaves it in err[1]);
 // the launch uses the smallest budget (2304, 4608 or 9216 bytes per warp) that covers it.
 void launch_numeric_rank_all(const long long* bin_off, long long m, int gidx, int max_need,

@@ -335,19 +335,20 @@ void launch_sym_warp(int bin, const int* rows, const long long* bin_off, Csr A, 
 // Small problems: warp per row over every row of A (no binning) computes the row's column span
 // and exact count in one pass with a bitmap of at most WORDS words, writes lo / hi for the rank
 // tier, and sets kErrSmallFallback (row_nnz 0) for a row whose bitmap or rank-tier layout would
-// not fit, after which the caller runs the general pipeline. Such a row also sets *stop (a word
-// on a cache line of its own, away from the per-row atomics on err), and every warp stops one row
-// after it sees it: the word is read at the start of a row and tested at the start of the next,
-// so the read's latency hides behind the row's work (the pass's results are then discarded, and
-// the general pipeline's analyze repeats the bounds check). bin_off receives {0, m}.
+// not fit, after which the caller runs the general pipeline. Such a row also raises a flag in its
+// CTA's shared memory, and the CTA's warps stop at their next row: the pass's results are then
+// discarded (the general pipeline's analyze repeats the bounds check). The flag is per CTA on
+// purpose: a global stop word polled by every warp on every row queues all those reads at one L2
+// slice and slowed the pass even when no row fell back. bin_off receives {0, m}.
 template <int WORDS, int WPB, int G>
 __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int upper,
                                                             int row_base, int* lo_arr,
                                                             int* hi_arr, int* row_nnz,
                                                             long long* bin_off,
                                                             unsigned long long* total_flop,
-                                                            int* err, int* stop) {
+                                                            int* err) {
   extern __shared__ unsigned sym_smem[];
+  __shared__ int cta_stop;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned* bm = sym_smem + warp * WORDS;
   const int m = A.rows;
@@ -355,10 +356,10 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
     bin_off[0] = 0;
     bin_off[1] = m;
   }
-  int stop_seen = 0;   // *stop as read at the start of the previous row
+  if (threadIdx.x == 0) cta_stop = 0;
+  __syncthreads();
   for (long long r = (long long)blockIdx.x * WPB + warp; r < m; r += (long long)gridDim.x * WPB) {
-    if (__shfl_sync(kFull, stop_seen, 0)) break;
-    stop_seen = *(volatile const int*)stop;
+    if (__shfl_sync(kFull, *(volatile int*)&cta_stop, 0)) break;
     const int i = (int)r;
     const int rs = A.rp[i], re = A.rp[i + 1];
     int lo = INT_MAX, hi = -1, bad = 0;
@@ -405,7 +406,7 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
     if (W > WORDS || 6ll * W + 20 > kRankMaxBudget) {
       if (lane == 0) {
         set_error(err, kErrSmallFallback);
-        *(volatile int*)stop = 1;
+        *(volatile int*)&cta_stop = 1;
         row_nnz[i] = 0;
       }
       continue;
@@ -423,7 +424,7 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
       const long long need = 6ll * W + 10ll * (cnt + 1);   // the row's rank-tier budget
       if (need > kRankMaxBudget) {
         set_error(err, kErrSmallFallback);
-        *(volatile int*)stop = 1;
+        *(volatile int*)&cta_stop = 1;
       } else {
         atomicMax(err + 1, (int)need);   // the numeric launch picks the smallest budget
       }
@@ -434,8 +435,8 @@ __global__ void __launch_bounds__(WPB * 32) sym_small_kernel(Csr A, Csr B, int u
 
 template <int G>
 void run_sym_small(Csr A, Csr B, int upper, int row_base, int* lo, int* hi, int* row_nnz,
-                   long long* bin_off, unsigned long long* total_flop, int* err, int* stop,
-                   int num_sms, cudaStream_t s) {
+                   long long* bin_off, unsigned long long* total_flop, int* err, int num_sms,
+                   cudaStream_t s) {
   constexpr int WORDS = 1536, WPB = 8;
   const size_t smem = (size_t)WORDS * WPB * sizeof(unsigned);
   auto kern = sym_small_kernel<WORDS, WPB, G>;
@@ -444,7 +445,7 @@ void run_sym_small(Csr A, Csr B, int upper, int row_base, int* lo, int* hi, int*
   if (blocks > (long long)num_sms * 4) blocks = (long long)num_sms * 4;
   if (blocks < 1) blocks = 1;
   kern<<<(unsigned)blocks, WPB * 32, smem, s>>>(A, B, upper, row_base, lo, hi, row_nnz, bin_off,
-                                                total_flop, err, stop);
+                                                total_flop, err);
 }
 
 }  // namespace
@@ -510,15 +511,15 @@ int build_dense_rows(Csr B, int* id, int* list, unsigned* bits, unsigned* pre, l
 
 void launch_symbolic_small(Csr A, Csr B, int upper, int row_base, int gidx, int* lo, int* hi,
                            int* row_nnz, long long* bin_off, unsigned long long* total_flop,
-                           int* err, int* stop, int num_sms, cudaStream_t s) {
+                           int* err, int num_sms, cudaStream_t s) {
   if (gidx == 2)
-    run_sym_small<4>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, stop,
+    run_sym_small<4>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err,
                      num_sms, s);
   else if (gidx == 1)
-    run_sym_small<2>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, stop,
+    run_sym_small<2>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err,
                      num_sms, s);
   else
-    run_sym_small<1>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err, stop,
+    run_sym_small<1>(A, B, upper, row_base, lo, hi, row_nnz, bin_off, total_flop, err,
                      num_sms, s);
 }
 
