@@ -74,6 +74,8 @@ def _wl(size: str = "full"):
             kw = PROFILE_SIZES[k]
             w["gen"] = (lambda g=gens[k], kw=kw: g(**kw))
             w["name"] = w["name"] + "_profile" + "".join(f"_{a}{b}" for a, b in kw.items())
+            if kw:
+                w["data"] += ", reduced: " + ", ".join(f"{a}={b}" for a, b in kw.items())
         return out
     return {
         "stencil27": {"name": "stencil27_64cube_AxA", "op": "ab",
