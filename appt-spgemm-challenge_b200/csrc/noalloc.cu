@@ -15,8 +15,7 @@
 // bytes per row of A); larger A is rejected with APPT_ERR_TOO_LARGE and a message.
 //
 // The first call on a device looks up the device address of the scratch array
-// (cudaGetSymbolAddress, with that device current) and caches it; make that first call before
-// any stream capture. Every call uses the same array and leaves its contents there; everything
+// (cudaGetSymbolAddress, with that device current) and caches it. Every call uses the same array and leaves its contents there; everything
 // a call relies on being zero it clears itself. Calls whose GPU work overlapped would race on the
 // array: this function serialises its callers per device on the host and returns only after its
 // own GPU work has finished, so calls made through it do not overlap. Each call blocks its host

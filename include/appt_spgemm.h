@@ -238,8 +238,7 @@ double appt_reference_score(const int32_t *row_ptr, int64_t rows, int64_t nnz);
  * C_capacity (size the buffers and call again). Temporaries live in one fixed 64 MiB device
  * array owned by the library (present on every GPU that loads it, until exit), which limits A
  * to about 2.2 million rows (larger A: APPT_ERR_TOO_LARGE with a message). The first call on a
- * device resolves that array's address and should come before any stream capture. Calls share
- * the array; this function serialises them per device and waits for its own GPU work: every call
+ * device resolves that array's address. Calls share the array; this function serialises them per device and waits for its own GPU work: every call
  * blocks its host thread (nnz(C) is read back mid-call and the stream is synchronised before it
  * returns). */
 int appt_spgemm_noalloc(const appt_csr *A, const appt_csr *B, int64_t *C_row_ptr,
