@@ -51,6 +51,42 @@ def test_small_problem_path_and_general_pipeline_agree(name, op, monkeypatch):
         assert np.array_equal(C1.val, C2.val)
 
 
+def _with_wide_rows(A, rows, per_row, seed):
+    """A copy of A whose given rows are replaced by `per_row` columns spread over all columns."""
+    rng = np.random.default_rng(seed)
+    rp = np.asarray(A.row_ptr, np.int64)
+    cols = [A.col_idx[rp[i]:rp[i + 1]] for i in range(A.rows)]
+    vals = [A.val[rp[i]:rp[i + 1]] for i in range(A.rows)]
+    for i in rows:
+        cols[i] = np.unique(rng.integers(0, A.cols, per_row)).astype(np.int32)
+        vals[i] = rng.uniform(-1, 1, cols[i].size)
+    nrp = np.zeros(A.rows + 1, np.int64)
+    nrp[1:] = np.cumsum([c.size for c in cols])
+    return M.Csr(A.rows, A.cols, nrp.astype(np.int32), np.concatenate(cols),
+                 np.concatenate(vals))
+
+
+@pytest.mark.parametrize("case", ["every_row_wide", "few_rows_wide"])
+def test_small_path_fallback_equals_general_pipeline(case, monkeypatch):
+    """A's rows are within the small-problem path's limit (2^17), but rows of C are too wide for
+    it: every row (uniform columns over 2^17) or the rows near a few planted wide rows of a
+    banded matrix. The path stops early and hands the call to the binned pipeline, whose result
+    must equal a call that skips the small path outright, bit for bit, and the oracle."""
+    n = 1 << 17
+    if case == "every_row_wide":
+        A = M.uniform8(n)
+    else:
+        A = _with_wide_rows(M.banded(n, per_row=8, half_width=64, seed=6), [5, 70000, 131000],
+                            8, seed=7)
+    C1, st1 = check(A)
+    monkeypatch.setenv("APPT_NO_SMALL_PATH", "1")
+    C2, st2 = check(A)
+    assert np.array_equal(C1.row_ptr, C2.row_ptr)
+    assert np.array_equal(C1.col_idx, C2.col_idx)
+    assert np.array_equal(C1.val, C2.val)
+    assert st1["tier_rows"] == st2["tier_rows"]
+
+
 @pytest.mark.parametrize("method", METHODS)
 @pytest.mark.parametrize("op", ["aat", "aat_upper"])
 def test_random_aat(method, op):
